@@ -1,0 +1,111 @@
+"""ctypes binding of the C ABI declared in ``include/fmoe.h``.
+
+The library is the in-tree ``flashinfer_b200/_lib/libfmoe.so`` built by
+``flashinfer_b200.build``. There is no fallback: if it is missing or does not
+load, importing the operator raises, so a silent CPU or library path can never
+stand in for the CUDA kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, Structure, byref, c_char_p, c_float, c_int32, c_int64, c_size_t, c_void_p
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libfmoe.so")
+
+FMOE_OK = 0
+ERRORS = {
+    -1: "FMOE_ERR_NULL: a required pointer is NULL",
+    -2: "FMOE_ERR_SHAPE: unsupported hidden/intermediate/expert/top-k sizes",
+    -3: "FMOE_ERR_ALIGN: a pointer is not 16-byte aligned",
+    -4: "FMOE_ERR_OFFSET: local_expert_offset + num_local_experts exceeds the expert count",
+    -5: "FMOE_ERR_WORKSPACE: workspace missing or too small",
+    -6: "FMOE_ERR_DTYPE: unsupported routing logits / bias dtype",
+    -7: "FMOE_ERR_CUDA: a CUDA runtime or driver call failed",
+    -8: "FMOE_ERR_DEVICE: the current device is not sm_100 (B200)",
+}
+DTYPE_F32 = 0
+DTYPE_BF16 = 1
+STOP_NONE, STOP_ROUTE, STOP_GATHER, STOP_GEMM1, STOP_GEMM2 = 0, 1, 2, 3, 4
+STATUS_TIMEOUT_GEMM1 = 0x1
+STATUS_TIMEOUT_GEMM2 = 0x2
+
+EXPORTS = ("fmoe_workspace_size", "fmoe_workspace_layout", "fmoe_run", "fmoe_route",
+           "fmoe_read_status", "fmoe_device_sm_count", "fmoe_version")
+
+
+class FmoeArgs(Structure):
+    _fields_ = [
+        ("routing_logits", c_void_p),
+        ("logits_dtype", c_int32),
+        ("routing_bias", c_void_p),
+        ("bias_dtype", c_int32),
+        ("hidden_states", c_void_p),
+        ("hidden_states_scale", c_void_p),
+        ("gemm1_weights", c_void_p),
+        ("gemm1_weights_scale", c_void_p),
+        ("gemm2_weights", c_void_p),
+        ("gemm2_weights_scale", c_void_p),
+        ("output", c_void_p),
+        ("num_tokens", c_int32),
+        ("hidden_size", c_int32),
+        ("intermediate_size", c_int32),
+        ("num_experts", c_int32),
+        ("num_local_experts", c_int32),
+        ("top_k", c_int32),
+        ("n_group", c_int32),
+        ("topk_group", c_int32),
+        ("local_expert_offset", c_int32),
+        ("routed_scaling_factor", c_float),
+        ("workspace", c_void_p),
+        ("workspace_bytes", c_size_t),
+        ("stop_after", c_int32),
+        ("phase_events", c_void_p),
+        ("num_phase_events", c_int32),
+    ]
+
+
+class FmoeLayout(Structure):
+    _fields_ = [(n, c_size_t) for n in (
+        "total_bytes", "status", "plan", "topk_ids", "topk_weights", "expert_count",
+        "expert_base", "slot_token", "slot_weight", "token_slot", "token_weight", "a_perm",
+        "a_scale_t", "h_hi", "h_lo", "h_scale_t", "y_rows", "partials", "counters")] + [
+        ("cap_slots", c_int64), ("max_units", c_int64)]
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Loads the library once; raises if it is absent (build it with flashinfer_b200.build)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build the CUDA library with `python -m flashinfer_b200.build`")
+    lib = ctypes.CDLL(LIB_PATH)
+    lib.fmoe_workspace_size.argtypes = [c_int32, c_int32, c_int32, c_int32, POINTER(c_size_t)]
+    lib.fmoe_workspace_layout.argtypes = [c_int32, c_int32, c_int32, c_int32, POINTER(FmoeLayout)]
+    lib.fmoe_run.argtypes = [POINTER(FmoeArgs), c_void_p]
+    lib.fmoe_route.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int32, c_int32, c_int32,
+                               c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]
+    lib.fmoe_read_status.argtypes = [c_void_p, c_void_p, POINTER(c_int32)]
+    lib.fmoe_device_sm_count.argtypes = [POINTER(c_int32)]
+    lib.fmoe_version.restype = c_char_p
+    for name in EXPORTS:
+        if name != "fmoe_version":
+            getattr(lib, name).restype = c_int32
+    _lib = lib
+    return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != FMOE_OK:
+        raise RuntimeError(f"{what} failed: {ERRORS.get(rc, f'error {rc}')}")
+
+
+def workspace_layout(T: int, e_local: int, hidden: int, inter: int) -> FmoeLayout:
+    lay = FmoeLayout()
+    check(load().fmoe_workspace_layout(T, e_local, hidden, inter, byref(lay)), "fmoe_workspace_layout")
+    return lay

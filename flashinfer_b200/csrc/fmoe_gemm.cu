@@ -1,0 +1,512 @@
+// fmoe_gemm.cu -- grouped FP8 e4m3 GEMMs with 128x128 block-scale promotion on tcgen05.
+//
+// Reference counterparts (solution/triton/kernel.py):
+//   KIND 1  <- _persistent_gemm1_kernel kernel.py:69-186 (+ _swiglu_kernel :301-330 fused in
+//              the epilogue; output re-encoded as two e4m3 terms with one scale per 128 cols)
+//   KIND 2  <- _persistent_gemm2_kernel kernel.py:193-293 (the reference runs this GEMM in
+//              TF32 on an fp32 intermediate; here A = hi + lo e4m3 terms, two MMAs per K block)
+//
+// Per CTA (persistent, one per SM, 320 threads):
+//   warp 0      TMA producer: A tile [128 slots x 128 K] (+ the lo term for KIND 2) and the
+//               weight tile [256 rows x 128 K] into an NS-stage shared-memory ring.
+//   warp 1      MMA issuer: per 128-wide K block, tcgen05.mma kind::f8f6f4 M=128 N=256 K=32
+//               x4 (x8 for KIND 2) into one of two TMEM partial buffers (2 x 256 columns).
+//   warps 2-9   promotion + epilogue: read each K block's partial from TMEM, scale it by
+//               a_scale[slot, kb] * w_scale[n-block, kb] and accumulate in fp32 registers
+//               (the reference's "partial * sa * sb" promotion, kernel.py:167-171).
+// Work unit = (tile, K split). Tiles are ordered expert -> n-tile -> m-tile so concurrently
+// running CTAs share weight tiles in L2. When there are fewer tiles than SMs, the K range is
+// split; every split writes its partial tile, and the last one to arrive (an atomic counter)
+// sums them in split order and runs the epilogue -- deterministic, and no CTA ever waits on
+// another.
+#include <cuda_bf16.h>
+
+#include "fmoe_internal.h"
+#include "fmoe_ptx.cuh"
+
+namespace fmoe {
+
+struct GemmArgs {
+  const int32_t* plan;
+  const int32_t* expert_base;
+  const int32_t* expert_count;
+  const float* a_scale_t;  // [nkb][cap]
+  const float* w_scale;    // KIND1 [E][2I/128][H/128], KIND2 [E][H/128][I/128]
+  float* partials;
+  int32_t* counters;
+  int32_t* status;
+  uint8_t* h_hi;
+  uint8_t* h_lo;
+  float* h_scale_t;        // [I/128][cap]
+  __nv_bfloat16* y;        // [cap][H]
+  int E, H, I;
+  int64_t cap;
+  int partial_rows;
+};
+
+template <int KIND>
+struct Cfg;
+template <>
+struct Cfg<1> {
+  static constexpr int NS = 4;
+  static constexpr int A_TILES = 1;
+  static constexpr int STAGE = 128 * 128 * A_TILES + 256 * 128;  // 48 KB
+};
+template <>
+struct Cfg<2> {
+  static constexpr int NS = 3;
+  static constexpr int A_TILES = 2;
+  static constexpr int STAGE = 128 * 128 * A_TILES + 256 * 128;  // 64 KB
+};
+
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr int kTmemCols = 512;
+constexpr int kATileBytes = 128 * 128;
+
+struct GemmTail {
+  uint64_t full[4];
+  uint64_t empty[4];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int last_flag;
+  int abort_flag;
+  int pad_;
+  float sb0[64];
+  float sb1[64];
+  float amax_x[2][128];
+  int ebase[kMaxLocalExperts + 1];
+  int ecnt[kMaxLocalExperts];
+};
+
+template <int KIND>
+constexpr size_t gemm_smem_bytes() {
+  return static_cast<size_t>(Cfg<KIND>::NS) * Cfg<KIND>::STAGE + sizeof(GemmTail) + 1024;
+}
+
+struct Unit {
+  int e, n, row0, nrows, kb0, kb1;
+};
+
+__device__ __forceinline__ Unit decode_unit(int unit, int S, int NT, int nkb, const int* ebase,
+                                            const int* ecnt, int E) {
+  const int tile = unit / S;
+  const int split = unit - tile * S;
+  int lo = 0, hi = E;
+  while (lo < hi) {  // first expert e with tile < tile_base(e + 1)
+    const int mid = (lo + hi) >> 1;
+    if (tile < (ebase[mid + 1] >> 7) * NT)
+      hi = mid;
+    else
+      lo = mid + 1;
+  }
+  const int e = lo < E ? lo : E - 1;
+  const int mt = max(1, (ebase[e + 1] - ebase[e]) >> 7);
+  const int local = tile - (ebase[e] >> 7) * NT;
+  const int n = local / mt;
+  const int m = local - n * mt;
+  Unit u;
+  u.e = e;
+  u.n = n;
+  u.row0 = ebase[e] + m * 128;
+  u.nrows = min(128, ecnt[e] - m * 128);
+  u.kb0 = split * nkb / S;
+  u.kb1 = (split + 1) * nkb / S;
+  return u;
+}
+
+// Bounded wait that also gives up when another role of this CTA has already aborted.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
+                                              volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((++spins & 127u) == 0) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > FMOE_WAIT_NS) return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void raise_abort(GemmTail* tail, int32_t* status, int code) {
+  *reinterpret_cast<volatile int*>(&tail->abort_flag) = 1;
+  atomicOr(status, code);
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
+           const __grid_constant__ CUtensorMap tm_w, const GemmArgs args) {
+  using C = Cfg<KIND>;
+  constexpr int NS = C::NS;
+  constexpr int STAGE = C::STAGE;
+  constexpr int kErr = KIND == 1 ? FMOE_STATUS_TIMEOUT_GEMM1 : FMOE_STATUS_TIMEOUT_GEMM2;
+
+  const int S = args.plan[KIND == 1 ? kPlanSplit1 : kPlanSplit2];
+  const int units = args.plan[KIND == 1 ? kPlanUnits1 : kPlanUnits2];
+  if (static_cast<int>(blockIdx.x) >= units) return;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  GemmTail* tail = reinterpret_cast<GemmTail*>(smem + NS * STAGE);
+  volatile int* abort_flag = &tail->abort_flag;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int E = args.E;
+  const int nkb = KIND == 1 ? args.H / kBlock : args.I / kBlock;
+  const int NT = KIND == 1 ? args.I / kBlock : args.H / kTileN;
+
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    tail->ebase[i] = args.expert_base[i];
+    if (i < E) tail->ecnt[i] = args.expert_count[i];
+  }
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&tail->full[s], 1);
+      mbar_init(&tail->empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tail->tfull[b], 1);
+      mbar_init(&tail->tempty[b], kEpiWarps);
+    }
+    mbar_init(&tail->drain, 1);
+    tail->abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tm_a0);
+    if (KIND == 2) tma_prefetch_desc(&tm_a1);
+    tma_prefetch_desc(&tm_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(&tail->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tail->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_a = policy_evict_last();
+      int last_round[NS];
+#pragma unroll
+      for (int s = 0; s < NS; ++s) last_round[s] = -1;
+      int it = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
+        const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
+        for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+          const int s = it % NS;
+          const int r = it / NS;
+          if (r > 0 && !wait_or_abort(&tail->empty[s], (r & 1) ^ 1, abort_flag)) {
+            raise_abort(tail, args.status, kErr);
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * STAGE;
+          mbar_arrive_expect_tx(&tail->full[s], STAGE);
+          const int kx = kb * kBlock;
+          if (KIND == 1) {
+            const int wrow = u.e * 2 * args.I + u.n * kBlock;
+            tma_load_2d(st, &tm_a0, &tail->full[s], kx, u.row0, pol_a);
+            tma_load_2d(st + kATileBytes, &tm_w, &tail->full[s], kx, wrow, pol_w);
+            tma_load_2d(st + 2 * kATileBytes, &tm_w, &tail->full[s], kx, wrow + args.I, pol_w);
+          } else {
+            const int wrow = u.e * args.H + u.n * kTileN;
+            tma_load_2d(st, &tm_a0, &tail->full[s], kx, u.row0, pol_a);
+            tma_load_2d(st + kATileBytes, &tm_a1, &tail->full[s], kx, u.row0, pol_a);
+            tma_load_2d(st + 2 * kATileBytes, &tm_w, &tail->full[s], kx, wrow, pol_w);
+          }
+          last_round[s] = r;
+        }
+      }
+      // Never leave a bulk copy in flight into shared memory that is about to be released.
+#pragma unroll
+      for (int s = 0; s < NS; ++s)
+        if (last_round[s] >= 0) (void)mbar_wait(&tail->full[s], last_round[s] & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
+      int it = 0, kt = 0;
+      bool ok = true;
+      for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
+        const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
+        for (int kb = u.kb0; kb < u.kb1; ++kb, ++it, ++kt) {
+          const int s = it % NS;
+          const int r = it / NS;
+          const int b = kt & 1;
+          const int rb = kt >> 1;
+          if (!wait_or_abort(&tail->full[s], r & 1, abort_flag) ||
+              (rb > 0 && !wait_or_abort(&tail->tempty[b], (rb & 1) ^ 1, abort_flag))) {
+            raise_abort(tail, args.status, kErr);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + b * kTileN;
+          const uint32_t st = smem_u32(smem + s * STAGE);
+          const uint64_t a_desc = smem_desc_k128(st);
+          const uint64_t b_desc = smem_desc_k128(st + C::A_TILES * kATileBytes);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)  // 4 x K=32 covers the 128-byte row
+            mma_f8f6f4(d, a_desc + 2 * j, b_desc + 2 * j, idesc, j > 0 ? 1u : 0u);
+          if (KIND == 2) {
+            const uint64_t lo_desc = smem_desc_k128(st + kATileBytes);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) mma_f8f6f4(d, lo_desc + 2 * j, b_desc + 2 * j, idesc, 1u);
+          }
+          mma_commit(&tail->empty[s]);
+          mma_commit(&tail->tfull[b]);
+        }
+      }
+      mma_commit(&tail->drain);
+      (void)mbar_wait(&tail->drain, 0);
+    }
+  } else {
+    // ------------------------------------------------------------------ promotion + epilogue
+    const int ew = warp - 2;
+    const int g = ew >> 2;        // column group: 0 -> cols [0,64)+[128,192), 1 -> [64,128)+...
+    const int q = warp & 3;       // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;  // tile row (slot) owned by this thread
+    const int etid = ew * 32 + lane;
+    const int64_t cap = args.cap;
+    int kt = 0;
+    bool ok = true;
+    float acc[128];
+    for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
+      const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
+      named_bar_sync(1, kEpiWarps * 32);
+      for (int i = etid; i < nkb; i += kEpiWarps * 32) {
+        if (KIND == 1) {
+          const int nb1 = args.I / kBlock;
+          const size_t base = static_cast<size_t>(u.e) * 2 * nb1;
+          tail->sb0[i] = __ldg(args.w_scale + (base + u.n) * nkb + i);
+          tail->sb1[i] = __ldg(args.w_scale + (base + nb1 + u.n) * nkb + i);
+        } else {
+          const size_t base = static_cast<size_t>(u.e) * (args.H / kBlock);
+          tail->sb0[i] = __ldg(args.w_scale + (base + 2 * u.n) * nkb + i);
+          tail->sb1[i] = __ldg(args.w_scale + (base + 2 * u.n + 1) * nkb + i);
+        }
+      }
+      named_bar_sync(1, kEpiWarps * 32);
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+      const float* sa_ptr = args.a_scale_t + u.row0 + r;
+      float sa_next = u.kb0 < u.kb1 ? __ldg(sa_ptr + static_cast<int64_t>(u.kb0) * cap) : 0.0f;
+      for (int kb = u.kb0; kb < u.kb1; ++kb, ++kt) {
+        const float sa = sa_next;
+        if (kb + 1 < u.kb1) sa_next = __ldg(sa_ptr + static_cast<int64_t>(kb + 1) * cap);
+        const int b = kt & 1;
+        const int rb = kt >> 1;
+        bool got = ok && wait_or_abort(&tail->tfull[b], rb & 1, abort_flag);
+        got = __all_sync(0xffffffffu, got);
+        if (!got && ok) {
+          if (lane == 0) raise_abort(tail, args.status, kErr);
+          ok = false;
+        }
+        if (got) {
+          tc_fence_after();
+          const float f0 = sa * tail->sb0[kb];
+          const float f1 = sa * tail->sb1[kb];
+          const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kTileN;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int col = (c < 2 ? 0 : 128) + g * 64 + (c & 1) * 32;
+            const float f = c < 2 ? f0 : f1;
+            float v[32];
+            tmem_ld_32x32b_x32(taddr + col, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(v[i], f, acc[c * 32 + i]);
+          }
+          tc_fence_before();
+        }
+        __syncwarp();
+        if (got && lane == 0) mbar_arrive(&tail->tempty[b]);
+      }
+
+      const bool valid = r < u.nrows;
+      if (S > 1) {
+        // split-K: publish this split's partial tile, the last arriver reduces in split order
+        const int tile = unit / S;
+        const int slot_rows = args.partial_rows;
+        if (valid) {
+          float* p = args.partials + (static_cast<size_t>(unit) * slot_rows + r) * kTileN;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float4* dst = reinterpret_cast<float4*>(p + h * 128 + g * 64);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              dst[i] = make_float4(acc[h * 64 + 4 * i], acc[h * 64 + 4 * i + 1],
+                                   acc[h * 64 + 4 * i + 2], acc[h * 64 + 4 * i + 3]);
+          }
+        }
+        __threadfence();
+        named_bar_sync(1, kEpiWarps * 32);
+        if (etid == 0) {
+          const int old = atomicAdd(args.counters + (KIND == 1 ? 0 : kMaxSplitUnits) + tile, 1);
+          tail->last_flag = (old == S - 1);
+        }
+        named_bar_sync(1, kEpiWarps * 32);
+        if (!tail->last_flag) continue;
+        __threadfence();
+        if (valid) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+          for (int sp = 0; sp < S; ++sp) {
+            const float* p =
+                args.partials + (static_cast<size_t>(tile * S + sp) * slot_rows + r) * kTileN;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const float4* src = reinterpret_cast<const float4*>(p + h * 128 + g * 64);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float4 v = __ldcg(src + i);
+                acc[h * 64 + 4 * i] += v.x;
+                acc[h * 64 + 4 * i + 1] += v.y;
+                acc[h * 64 + 4 * i + 2] += v.z;
+                acc[h * 64 + 4 * i + 3] += v.w;
+              }
+            }
+          }
+        }
+      }
+
+      if (KIND == 1) {
+        // SwiGLU (moe.py:90-92: silu(second half) * first half), then the two-term e4m3
+        // encoding with one scale per slot per 128 intermediate columns.
+        float amax = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float gate = acc[c];
+          const float up = acc[64 + c];
+          const float h = valid ? (up / (1.0f + expf(-up))) * gate : 0.0f;
+          acc[c] = h;
+          amax = fmaxf(amax, fabsf(h));
+        }
+        tail->amax_x[g][r] = amax;
+        named_bar_sync(1, kEpiWarps * 32);
+        amax = fmaxf(tail->amax_x[0][r], tail->amax_x[1][r]);
+        const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
+        const float scale = amax / 448.0f;
+        const size_t row = static_cast<size_t>(u.row0) + r;
+        uint4* hi_dst =
+            reinterpret_cast<uint4*>(args.h_hi + row * args.I + u.n * kBlock + g * 64);
+        uint4* lo_dst =
+            reinterpret_cast<uint4*>(args.h_lo + row * args.I + u.n * kBlock + g * 64);
+#pragma unroll
+        for (int v16 = 0; v16 < 4; ++v16) {
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            uint32_t hbits = 0, lbits = 0;
+#pragma unroll
+            for (int pr = 0; pr < 2; ++pr) {
+              const int c = v16 * 16 + w * 4 + pr * 2;
+              const float x0 = acc[c] * inv;
+              const float x1 = acc[c + 1] * inv;
+              const uint16_t hp = pack_e4m3x2(x0, x1);
+              const float2 back = unpack_e4m3x2(hp);
+              const uint16_t lp = pack_e4m3x2(x0 - back.x, x1 - back.y);
+              hbits |= static_cast<uint32_t>(hp) << (16 * pr);
+              lbits |= static_cast<uint32_t>(lp) << (16 * pr);
+            }
+            hw[w] = hbits;
+            lw[w] = lbits;
+          }
+          hi_dst[v16] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          lo_dst[v16] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+        if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = scale;
+      } else {
+        if (valid) {
+          const size_t row = static_cast<size_t>(u.row0) + r;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint4* dst = reinterpret_cast<uint4*>(args.y + row * args.H + u.n * kTileN + h * 128 +
+                                                  g * 64);
+#pragma unroll
+            for (int v8 = 0; v8 < 8; ++v8) {
+              uint32_t wv[4];
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                const __nv_bfloat162 pr = __floats2bfloat162_rn(acc[h * 64 + v8 * 8 + 2 * w],
+                                                                acc[h * 64 + v8 * 8 + 2 * w + 1]);
+                wv[w] = *reinterpret_cast<const uint32_t*>(&pr);
+              }
+              dst[v8] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int KIND>
+static cudaError_t launch_gemm_kind(const RunParams& p, const CUtensorMap& a0,
+                                    const CUtensorMap& a1, const CUtensorMap& w,
+                                    cudaStream_t s) {
+  const size_t smem = gemm_smem_bytes<KIND>();
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  uint8_t* ws = p.ws;
+  const Layout& L = p.L;
+  GemmArgs a{};
+  a.plan = reinterpret_cast<const int32_t*>(ws + L.plan);
+  a.expert_base = reinterpret_cast<const int32_t*>(ws + L.expert_base);
+  a.expert_count = reinterpret_cast<const int32_t*>(ws + L.expert_count);
+  a.a_scale_t = reinterpret_cast<const float*>(ws + (KIND == 1 ? L.a_scale_t : L.h_scale_t));
+  a.w_scale = KIND == 1 ? p.w1_scale : p.w2_scale;
+  a.partials = reinterpret_cast<float*>(ws + L.partials);
+  a.counters = reinterpret_cast<int32_t*>(ws + L.counters);
+  a.status = reinterpret_cast<int32_t*>(ws + L.status);
+  a.h_hi = ws + L.h_hi;
+  a.h_lo = ws + L.h_lo;
+  a.h_scale_t = reinterpret_cast<float*>(ws + L.h_scale_t);
+  a.y = reinterpret_cast<__nv_bfloat16*>(ws + L.y_rows);
+  a.E = p.E;
+  a.H = p.H;
+  a.I = p.I;
+  a.cap = L.cap;
+  a.partial_rows = static_cast<int>(L.partial_rows);
+  k_gemm<KIND><<<p.num_sms, kThreads, smem, s>>>(a0, a1, w, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUtensorMap& tm_w1,
+                         cudaStream_t s) {
+  return launch_gemm_kind<1>(p, tm_a, tm_a, tm_w1, s);
+}
+
+cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
+                         const CUtensorMap& tm_w2, cudaStream_t s) {
+  return launch_gemm_kind<2>(p, tm_hi, tm_lo, tm_w2, s);
+}
+
+}  // namespace fmoe

@@ -1,0 +1,117 @@
+// fmoe_internal.h -- shared constants, workspace layout and kernel launch declarations.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/fmoe.h"
+
+namespace fmoe {
+
+constexpr int kBlock = 128;          // scale block edge (activations: per token per 128 K;
+                                     // weights: 128x128)
+constexpr int kTopK = 8;
+constexpr int kGroups = 8;
+constexpr int kTopKGroups = 4;
+constexpr int kExpertsGlobal = 256;
+constexpr int kMaxLocalExperts = 256;
+constexpr int kTileM = 128;          // slots per GEMM tile (one expert per tile)
+constexpr int kTileN = 256;          // weight rows per GEMM tile
+constexpr int kMaxSplitUnits = 1024; // split-K partial tiles the workspace holds
+constexpr int kMaxSplit = 8;
+
+// Plan header words (int32, written by the plan kernel).
+enum PlanWord {
+  kPlanPairs = 0,      // P: routed (token, local expert) pairs
+  kPlanPadded = 1,     // slots incl. per-expert padding to 128
+  kPlanMTiles = 2,     // 128-slot tiles
+  kPlanSplit1 = 3,     // GEMM1 K splits
+  kPlanUnits1 = 4,     // GEMM1 work units = tiles1 * split1
+  kPlanSplit2 = 5,
+  kPlanUnits2 = 6,
+  kPlanTiles1 = 7,
+  kPlanTiles2 = 8,
+  kPlanWords = 16,
+};
+
+struct Layout {
+  size_t total;
+  size_t status, plan, topk_ids, topk_w, expert_count, expert_base, slot_token, slot_weight;
+  size_t token_slot, token_weight, a_perm, a_scale_t, h_hi, h_lo, h_scale_t, y_rows;
+  size_t partials, counters;
+  int64_t cap;          // padded slot capacity
+  int64_t partial_rows; // rows stored per split-K partial tile (<= 128)
+};
+
+// Host + device: compute the workspace layout.
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+__host__ __device__ inline Layout make_layout(int T, int E, int H, int I) {
+  Layout L{};
+  const int64_t picks = (int64_t)(E < kTopK ? E : kTopK);
+  const int64_t pmax = (int64_t)T * picks;
+  const int64_t pad = 127 * (pmax < E ? pmax : (int64_t)E);
+  L.cap = (int64_t)align_up((size_t)(pmax + pad), kTileM);
+  L.partial_rows = T < kTileM ? (T > 0 ? T : 1) : kTileM;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o = align_up(o + bytes, 256);
+    return at;
+  };
+  L.status = take(16);
+  L.plan = take(kPlanWords * 4);
+  L.topk_ids = take((size_t)T * kTopK * 4);
+  L.topk_w = take((size_t)T * kTopK * 4);
+  L.expert_count = take((size_t)E * 4);
+  L.expert_base = take((size_t)(E + 1) * 4);
+  L.slot_token = take((size_t)L.cap * 4);
+  L.slot_weight = take((size_t)L.cap * 4);
+  L.token_slot = take((size_t)T * kTopK * 4);
+  L.token_weight = take((size_t)T * kTopK * 4);
+  L.a_perm = take((size_t)L.cap * H);
+  L.a_scale_t = take((size_t)(H / kBlock) * L.cap * 4);
+  L.h_hi = take((size_t)L.cap * I);
+  L.h_lo = take((size_t)L.cap * I);
+  L.h_scale_t = take((size_t)(I / kBlock) * L.cap * 4);
+  L.y_rows = take((size_t)L.cap * H * 2);
+  L.partials = take((size_t)kMaxSplitUnits * L.partial_rows * kTileN * 4);
+  L.counters = take((size_t)2 * kMaxSplitUnits * 4);
+  L.total = o;
+  return L;
+}
+
+struct RunParams {
+  // inputs
+  const void* logits;
+  int logits_dtype;
+  const void* bias;
+  int bias_dtype;
+  const uint8_t* hidden;
+  const float* hidden_scale;   // [H/128, T]
+  const float* w1_scale;       // [E, 2I/128, H/128]
+  const float* w2_scale;       // [E, H/128, I/128]
+  __nv_bfloat16* output;       // [T, H]
+  int T, H, I, E, local_start;
+  float rsf;
+  // workspace
+  uint8_t* ws;
+  Layout L;
+  int num_sms;
+};
+
+// Launchers (fmoe_kernels.cu / fmoe_gemm.cu). Return cudaGetLastError() of the launch.
+cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias, int bias_dtype,
+                         int T, float rsf, int32_t* topk_ids, float* topk_w, cudaStream_t s);
+cudaError_t launch_plan(const RunParams& p, cudaStream_t s);
+cudaError_t launch_gather(const RunParams& p, cudaStream_t s);
+cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUtensorMap& tm_w1,
+                         cudaStream_t s);
+cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
+                         const CUtensorMap& tm_w2, cudaStream_t s);
+cudaError_t launch_combine(const RunParams& p, cudaStream_t s);
+
+}  // namespace fmoe

@@ -1,0 +1,222 @@
+"""GPU parity of the sm_100a path (through the C ABI) against the CPU oracle.
+
+Bars (from the operator's benchmark contract):
+  * routing ids and the permutation: bit-exact;
+  * routing weights: bit-exact against the oracle (same arithmetic), <= 1e-6 relative
+    against the reference's golden weights;
+  * bf16 output: atol = rtol = 1e-2 against the fp32 oracle, on every element.
+"""
+import numpy as np
+import pytest
+import torch
+
+from flashinfer_b200 import _lib
+from flashinfer_b200 import moe as fmoe
+from flashinfer_b200 import workload as wl
+from oracle import moe as omoe
+from oracle import routing as orouting
+from tests.conftest import oracle_weights_for
+from tests.golden.make_golden import EP_CONFIGS, FULL_OUTPUT
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 1e-2
+RTOL = 1e-2
+ALL = dict(wl.CONFIGS)
+ALL.update(EP_CONFIGS)
+
+
+def to_gpu(act):
+    return (act.routing_logits.cuda(), act.routing_bias.cuda(), act.hidden_states.cuda(),
+            act.hidden_states_scale.cuda())
+
+
+def oracle_rows(act, cfg, rows, cpu_weights, local_start=0, e_local=32):
+    ids, w = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), cfg.rsf)
+    ids, w = ids[rows], w[rows]
+    active = sorted({int(e) - local_start for e in ids.reshape(-1)
+                     if 0 <= int(e) - local_start < e_local})
+    W1, s1, W2, s2 = oracle_weights_for(cpu_weights, active)
+    hs = act.hidden_states.view(torch.uint8).numpy()[rows]
+    sc = act.hidden_states_scale.numpy()[:, rows]
+    return omoe.moe_reference(hs, sc, W1, s1, W2, s2, ids, w, local_start)
+
+
+def run_gpu(act, gpu_weights, cfg, local_start=0, stop=_lib.STOP_NONE):
+    lg, b, hs, sc = to_gpu(act)
+    w1, s1, w2, s2 = gpu_weights
+    out, ws, lay = fmoe._launch(lg, b, hs, sc, w1, s1, w2, s2, local_start, cfg.rsf, None,
+                                stop_after=stop)
+    torch.cuda.synchronize()
+    assert fmoe.read_status(ws) == 0
+    return out, ws, lay
+
+
+@pytest.mark.parametrize("name", sorted(ALL))
+def test_routing_bit_exact(name, golden_routing):
+    cfg = ALL[name]
+    act = cfg.activations()
+    ids, w = fmoe.route(act.routing_logits.cuda(), act.routing_bias.cuda(), cfg.rsf)
+    ids, w = ids.cpu().numpy(), w.cpu().numpy()
+    oids, ow = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), cfg.rsf)
+    np.testing.assert_array_equal(ids, oids)
+    np.testing.assert_array_equal(w.view(np.uint32), ow.view(np.uint32))
+    np.testing.assert_array_equal(np.sort(ids, axis=1), golden_routing[f"{name}/ids"].astype(np.int32))
+
+
+def test_routing_bf16_logits_and_fp32_bias():
+    cfg = wl.CONFIGS["t1024_s6"]
+    act = cfg.activations()
+    lg = act.routing_logits.to(torch.bfloat16)
+    b = act.routing_bias.float()
+    ids, w = fmoe.route(lg.cuda(), b.cuda(), cfg.rsf)
+    oids, ow = orouting.route(lg.float().numpy(), b.numpy(), cfg.rsf)
+    np.testing.assert_array_equal(ids.cpu().numpy(), oids)
+    np.testing.assert_array_equal(w.cpu().numpy().view(np.uint32), ow.view(np.uint32))
+
+
+@pytest.mark.parametrize("name,local_start", [("t16_s0", 0), ("t256_s5_skew", 0),
+                                              ("t1024_s6", 0), ("t16384_s9", 0),
+                                              ("ep_t16384_s10", 96)])
+def test_permutation_bit_exact(name, local_start, gpu_weights):
+    cfg = ALL[name]
+    act = cfg.activations()
+    _, ws, lay = run_gpu(act, gpu_weights, cfg, local_start=local_start, stop=_lib.STOP_ROUTE)
+    view = fmoe.WorkspaceView(ws, lay, cfg.T, 32, wl.HIDDEN, wl.INTER)
+    oids, ow = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), cfg.rsf)
+    lid, lw = orouting.local_view(oids, ow, local_start, 32)
+    counts, offsets, stoks, sw = orouting.permute(lid, lw, 32)
+    np.testing.assert_array_equal(view.expert_count().cpu().numpy(), counts)
+    base = view.expert_base().cpu().numpy()
+    slot_tok = view.slot_token().cpu().numpy()
+    slot_w = view.slot_weight().cpu().numpy()
+    plan = view.plan().cpu().numpy()
+    assert plan[0] == counts.sum()
+    assert plan[1] == base[-1] == sum((c + 127) // 128 * 128 for c in counts)
+    for e in range(32):
+        seg = slice(base[e], base[e] + counts[e])
+        np.testing.assert_array_equal(slot_tok[seg], stoks[offsets[e]:offsets[e + 1]])
+        np.testing.assert_array_equal(slot_w[seg].view(np.uint32),
+                                      sw[offsets[e]:offsets[e + 1]].view(np.uint32))
+        assert np.all(slot_tok[base[e] + counts[e]:base[e + 1]] == -1)
+    # token -> slot map: local picks in ascending expert order, -1 afterwards
+    ts = view.token_slot().cpu().numpy()
+    for t in range(0, cfg.T, max(1, cfg.T // 257)):
+        exp = sorted(int(e) for e in lid[t] if e >= 0)
+        got = [int(s) for s in ts[t] if s >= 0]
+        assert len(got) == len(exp)
+        for s, e in zip(got, exp):
+            assert base[e] <= s < base[e] + counts[e] and slot_tok[s] == t
+
+
+@pytest.mark.parametrize("name", sorted(FULL_OUTPUT))
+def test_output_matches_oracle_and_golden(name, gpu_weights, cpu_weights, golden_outputs):
+    cfg = wl.CONFIGS[name]
+    act = cfg.activations()
+    out, _, _ = run_gpu(act, gpu_weights, cfg)
+    bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
+    rows = FULL_OUTPUT[name] or cfg.T
+    sel = np.arange(rows)
+    ref = oracle_rows(act, cfg, sel, cpu_weights)
+    frac, err = omoe.allclose_report(bits[sel], ref, atol=ATOL, rtol=RTOL)
+    assert frac == 1.0, (frac, err)
+    gold = golden_outputs[f"{name}/out"]
+    frac, err = omoe.allclose_report(bits[:gold.shape[0]], gold, atol=ATOL, rtol=RTOL)
+    assert frac == 1.0, (frac, err)
+
+
+@pytest.mark.parametrize("name", ["t32_s3", "t256_s5", "t1024_s6_skew", "t4096_s7", "t16384_s9"])
+def test_output_sampled_rows(name, gpu_weights, cpu_weights):
+    """Large T: every token's output depends only on its own row and routing, so the oracle
+    checks a seeded sample of rows (plus the first and last token)."""
+    cfg = wl.CONFIGS[name]
+    act = cfg.activations()
+    out, _, _ = run_gpu(act, gpu_weights, cfg)
+    bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
+    rng = np.random.default_rng(cfg.seed)
+    sel = np.unique(np.concatenate([[0, cfg.T - 1], rng.choice(cfg.T, size=min(cfg.T, 24),
+                                                                replace=False)]))
+    ref = oracle_rows(act, cfg, sel, cpu_weights)
+    frac, err = omoe.allclose_report(bits[sel], ref, atol=ATOL, rtol=RTOL)
+    assert frac == 1.0, (frac, err)
+    assert np.isfinite(out.float().cpu().numpy()).all()
+
+
+def test_deterministic_bits(gpu_weights):
+    cfg = wl.CONFIGS["t1024_s6_skew"]
+    act = cfg.activations()
+    a, _, _ = run_gpu(act, gpu_weights, cfg)
+    a = a.clone()
+    b, _, _ = run_gpu(act, gpu_weights, cfg)
+    assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+def test_intermediate_two_term_encoding(gpu_weights, cpu_weights):
+    """GEMM1 + SwiGLU output, decoded as (hi + lo) * scale, against the oracle's fp32 h."""
+    cfg = wl.CONFIGS["t64_s4"]
+    act = cfg.activations()
+    _, ws, lay = run_gpu(act, gpu_weights, cfg, stop=_lib.STOP_GEMM1)
+    view = fmoe.WorkspaceView(ws, lay, cfg.T, 32, wl.HIDDEN, wl.INTER)
+    hi, lo, sc = (t.cpu() for t in view.intermediate())
+    slot_tok = view.slot_token().cpu().numpy()
+    base = view.expert_base().cpu().numpy()
+    from oracle.fp8 import e4m3_to_f32
+    A = omoe.dequant_activations(act.hidden_states.view(torch.uint8).numpy(),
+                                 act.hidden_states_scale.numpy())
+    checked = 0
+    for e in range(32):
+        slots = [s for s in range(base[e], base[e + 1]) if slot_tok[s] >= 0][:4]
+        if not slots:
+            continue
+        W1, s1, _, _ = oracle_weights_for(cpu_weights, [e])
+        W13 = omoe.dequant_weight(W1[e], s1[e])
+        g1 = A[slot_tok[slots]] @ W13.T
+        gate, up = g1[:, :wl.INTER], g1[:, wl.INTER:]
+        h = up / (1 + np.exp(-up)) * gate
+        dec = (e4m3_to_f32(hi[slots].numpy()) + e4m3_to_f32(lo[slots].numpy())) * \
+            np.repeat(sc[:, slots].numpy().T, 128, axis=1)
+        amax = np.abs(h).max()
+        np.testing.assert_allclose(dec, h, rtol=2e-2, atol=2e-3 * amax)
+        checked += 1
+        if checked >= 4:
+            break
+    assert checked > 0
+
+
+def test_no_local_pairs_gives_zeros(gpu_weights):
+    """All picks outside the local range: P = 0, output zero-filled (kernel.py:692-695)."""
+    act = wl.make_activations(8, 123)
+    act.routing_logits[:, 64:96] -= 30.0  # sigmoid ~ 0: the local range can never win
+    cfg = wl.Config("nolocal", 8, 123)
+    out, ws, lay = run_gpu(act, gpu_weights, cfg, local_start=64)
+    view = fmoe.WorkspaceView(ws, lay, 8, 32, wl.HIDDEN, wl.INTER)
+    assert int(view.plan()[0]) == 0
+    assert torch.count_nonzero(out.float()) == 0
+
+
+def test_all_tokens_on_one_expert(gpu_weights, cpu_weights):
+    """300 tokens all select local expert 5 (3 m-tiles, the last one ragged)."""
+    T = 300
+    act = wl.make_activations(T, 77)
+    act.routing_logits[:, 5] += 30.0      # sigmoid ~ 1 ...
+    act.routing_bias[5] = 1.0             # ... and a bias no other expert can reach
+    cfg = wl.Config("hot5", T, 77)
+    out, ws, lay = run_gpu(act, gpu_weights, cfg)
+    view = fmoe.WorkspaceView(ws, lay, T, 32, wl.HIDDEN, wl.INTER)
+    assert int(view.expert_count()[5]) == T
+    bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
+    sel = np.array([0, 1, 127, 128, 255, 256, 299])
+    ref = oracle_rows(act, cfg, sel, cpu_weights)
+    frac, err = omoe.allclose_report(bits[sel], ref, atol=ATOL, rtol=RTOL)
+    assert frac == 1.0, (frac, err)
+
+
+def test_output_written_in_place(gpu_weights):
+    cfg = wl.CONFIGS["t8_s2"]
+    act = cfg.activations()
+    lg, b, hs, sc = to_gpu(act)
+    w1, s1, w2, s2 = gpu_weights
+    out = torch.full((cfg.T, wl.HIDDEN), 7.0, dtype=torch.bfloat16, device="cuda")
+    ret = fmoe.run(lg, b, hs, sc, w1, s1, w2, s2, 0, cfg.rsf, out)
+    assert ret.data_ptr() == out.data_ptr()
+    assert not torch.any(out == 7.0)

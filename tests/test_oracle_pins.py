@@ -1,0 +1,112 @@
+"""Pins the CPU oracle to the operator's own PyTorch reference (golden vectors), no GPU.
+
+The golden files come from running the definition reference
+(``flashinfer/trace/templates/moe.py:109-184``) on the seeded workloads; see
+``tests/golden/make_golden.py``.
+"""
+import numpy as np
+import pytest
+import torch
+
+from flashinfer_b200 import workload as wl
+from oracle import moe as omoe
+from oracle import routing as orouting
+from oracle.fp8 import bf16_round, bf16_to_f32, e4m3_to_f32, round_e4m3
+from tests.conftest import oracle_weights_for
+from tests.golden.make_golden import EP_CONFIGS, FULL_OUTPUT
+
+ALL = dict(wl.CONFIGS)
+ALL.update(EP_CONFIGS)
+
+
+@pytest.mark.parametrize("name", sorted(ALL))
+def test_oracle_routing_matches_reference(name, golden_routing):
+    cfg = ALL[name]
+    act = cfg.activations()
+    ids, w = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), cfg.rsf)
+    order = np.argsort(ids, axis=1, kind="stable")
+    sid = np.take_along_axis(ids, order, 1)
+    gid = golden_routing[f"{name}/ids"].astype(np.int32)
+    assert sid.shape == gid.shape
+    np.testing.assert_array_equal(sid, gid)  # bit-exact per-token id sets
+    key = f"{name}/weights"
+    if key in golden_routing:
+        sw = np.take_along_axis(w, order, 1)
+        # the reference sums the 8 scores in torch's reduction order: weights agree to ~2 ulp
+        np.testing.assert_allclose(sw, golden_routing[key], rtol=1e-6, atol=0)
+
+
+def test_oracle_permutation_is_canonical():
+    cfg = wl.CONFIGS["t256_s5_skew"]
+    act = cfg.activations()
+    ids, w = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), cfg.rsf)
+    lid, lw = orouting.local_view(ids, w, 0, 32)
+    counts, offsets, stoks, sw = orouting.permute(lid, lw, 32)
+    assert counts.sum() == (lid >= 0).sum() == stoks.size
+    for e in range(32):
+        seg = stoks[offsets[e]:offsets[e + 1]]
+        assert np.all(np.diff(seg) > 0)  # ascending tokens within each expert
+        assert np.all((lid[seg] == e).any(axis=1))
+
+
+@pytest.mark.parametrize("name", sorted(FULL_OUTPUT))
+def test_oracle_forward_matches_reference(name, golden_outputs, cpu_weights):
+    cfg = wl.CONFIGS[name]
+    rows = FULL_OUTPUT[name]
+    act = cfg.activations()
+    ids, w = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), cfg.rsf)
+    if rows is not None:
+        ids, w = ids[:rows], w[:rows]
+    active = sorted({int(e) for e in ids.reshape(-1) if 0 <= e < 32})
+    W1, s1, W2, s2 = oracle_weights_for(cpu_weights, active)
+    hs = act.hidden_states.view(torch.uint8).numpy()
+    sc = act.hidden_states_scale.numpy()
+    if rows is not None:
+        hs, sc = hs[:rows], sc[:, :rows]
+    got = omoe.moe_reference(hs, sc, W1, s1, W2, s2, ids, w, 0)
+    ref = golden_outputs[f"{name}/out"]
+    # Same fp32 algorithm; only BLAS summation order differs, so every element agrees to
+    # within one bf16 ulp (relative 2^-8..2^-7) and almost all agree exactly.
+    frac, maxerr = omoe.allclose_report(got, ref, atol=1e-5, rtol=2.0 ** -7)
+    assert frac == 1.0, (frac, maxerr)
+    assert np.mean(got == ref) > 0.99
+
+
+def test_e4m3_codec_roundtrip():
+    raw = np.arange(256, dtype=np.uint8)
+    vals = e4m3_to_f32(raw)
+    finite = ~np.isnan(vals)
+    np.testing.assert_array_equal(round_e4m3(vals[finite]), vals[finite])
+    ref = torch.from_numpy(raw).view(torch.float8_e4m3fn).float().numpy()
+    np.testing.assert_array_equal(vals[finite], ref[finite])
+    x = np.random.default_rng(0).standard_normal(10000).astype(np.float32) * 100
+    ours = round_e4m3(x)
+    theirs = torch.from_numpy(np.clip(x, -448, 448)).to(torch.float8_e4m3fn).float().numpy()
+    np.testing.assert_array_equal(ours, theirs)
+
+
+def test_bf16_rounding_matches_torch():
+    x = np.random.default_rng(1).standard_normal(10000).astype(np.float32) * 3
+    ours = bf16_round(x)
+    theirs = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    np.testing.assert_array_equal(ours, theirs)
+    np.testing.assert_array_equal(bf16_to_f32(ours), torch.from_numpy(x).bfloat16().float().numpy())
+
+
+def test_two_term_intermediate_meets_tolerance(golden_outputs, cpu_weights):
+    """The device arithmetic (two-term e4m3 intermediate, bf16 Y rows) stays within
+    atol=rtol=1e-2 of the reference at T=16; a single e4m3 term would not."""
+    cfg = wl.CONFIGS["t16_s0"]
+    act = cfg.activations()
+    ids, w = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), cfg.rsf)
+    active = sorted({int(e) for e in ids.reshape(-1) if 0 <= e < 32})
+    W1, s1, W2, s2 = oracle_weights_for(cpu_weights, active)
+    hs = act.hidden_states.view(torch.uint8).numpy()
+    sc = act.hidden_states_scale.numpy()
+    ref = golden_outputs["t16_s0/out"]
+    dev = omoe.moe_device_numerics(hs, sc, W1, s1, W2, s2, ids, w, 0)
+    frac, _ = omoe.allclose_report(dev, ref)
+    assert frac == 1.0
+    single = omoe.moe_device_numerics(hs, sc, W1, s1, W2, s2, ids, w, 0, two_term=False)
+    frac1, _ = omoe.allclose_report(single, ref)
+    assert frac1 < 0.95
