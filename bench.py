@@ -30,7 +30,7 @@ sys.path.insert(0, ROOT)
 from flashinfer_b200 import _lib, moe as fmoe, workload as wl  # noqa: E402
 
 METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
-KERNELS_PER_CALL = 6   # route, plan, gather, gemm1, gemm2, combine
+KERNELS_PER_CALL = 7   # route+hist, scan, scatter, gather, gemm1, gemm2, combine
 
 
 def measured_peaks():
@@ -289,11 +289,16 @@ def main():
     ap.add_argument("--workload", default="t64_s4")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="run warm-up calls plus one call of --workload on GPU 0 and exit "
+                         "(the command the committed ncu summaries capture)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
     if args.impl == "reference":
         return reference_arm(args)
+    if args.profile:
+        return profile_once(args)
 
     world, rank, local = dist_setup(args.gpus)
     device = torch.device("cuda", local if world > 1 else 0)
@@ -411,6 +416,15 @@ def main():
         dist.destroy_process_group()
     if result is not None:
         print(json.dumps(result), flush=True)
+
+
+def profile_once(args):
+    device = torch.device("cuda", 0)
+    cfg = wl.CONFIGS[args.workload]
+    weights = tuple(t.to(device) for t in wl.local_weights(32, 0))
+    _, inp = make_inputs(cfg, device)
+    time_calls(inp, weights, 0, cfg.rsf, args.warmup + 1, phase=False)
+    torch.cuda.synchronize()
 
 
 def reference_arm(args):

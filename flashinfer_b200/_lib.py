@@ -69,8 +69,10 @@ class FmoeLayout(Structure):
     _fields_ = [(n, c_size_t) for n in (
         "total_bytes", "status", "plan", "topk_ids", "topk_weights", "expert_count",
         "expert_base", "slot_token", "slot_weight", "token_slot", "token_weight", "a_perm",
-        "a_scale_t", "h_hi", "h_lo", "h_scale_t", "y_rows", "partials", "counters")] + [
-        ("cap_slots", c_int64), ("max_units", c_int64)]
+        "a_scale_t", "h_hi", "h_lo", "h_scale_t", "y_rows", "y_scale", "partials", "counters",
+        "block_hist", "block_off")] + [
+        ("cap_slots", c_int64), ("max_units", c_int64), ("tokens_per_block", c_int64),
+        ("num_blocks", c_int64)]
 
 
 _lib = None

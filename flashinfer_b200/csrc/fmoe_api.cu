@@ -150,10 +150,15 @@ int fmoe_workspace_layout(int32_t T, int32_t E, int32_t H, int32_t I, FmoeLayout
   out->h_lo = L.h_lo;
   out->h_scale_t = L.h_scale_t;
   out->y_rows = L.y_rows;
+  out->y_scale = L.y_scale;
   out->partials = L.partials;
   out->counters = L.counters;
+  out->block_hist = L.block_hist;
+  out->block_off = L.block_off;
   out->cap_slots = L.cap;
   out->max_units = kMaxSplitUnits;
+  out->tokens_per_block = L.tpb;
+  out->num_blocks = L.nblocks;
   return FMOE_OK;
 }
 
@@ -228,15 +233,11 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
     return cudaEventRecord(static_cast<cudaEvent_t>(a->phase_events[i]), s) == cudaSuccess;
   };
   if (!mark(0)) return FMOE_ERR_CUDA;
-  // The plan kernel clears the status word before any GEMM can set it.
-  if (launch_route(p.logits, p.logits_dtype, p.bias, p.bias_dtype, T, p.rsf,
-                   reinterpret_cast<int32_t*>(p.ws + L.topk_ids),
-                   reinterpret_cast<float*>(p.ws + L.topk_w), s) != cudaSuccess)
+  // The scan kernel clears the status word before any GEMM can set it.
+  if (launch_route_hist(p, s) != cudaSuccess || launch_scan(p, s) != cudaSuccess || !mark(1))
     return FMOE_ERR_CUDA;
-  if (launch_plan(p, s) != cudaSuccess || !mark(1)) return FMOE_ERR_CUDA;
-  if (a->stop_after == FMOE_STOP_ROUTE) return FMOE_OK;
-  if (launch_gather(p, s) != cudaSuccess || !mark(2)) return FMOE_ERR_CUDA;
-  if (a->stop_after == FMOE_STOP_GATHER) return FMOE_OK;
+  if (launch_scatter_gather(p, s) != cudaSuccess || !mark(2)) return FMOE_ERR_CUDA;
+  if (a->stop_after == FMOE_STOP_ROUTE || a->stop_after == FMOE_STOP_GATHER) return FMOE_OK;
 
   CUtensorMap tm_a, tm_w1, tm_hi, tm_lo, tm_w2;
   if (!make_tmap_u8(&tm_a, p.ws + L.a_perm, H, L.cap, H, 128, 128) ||

@@ -20,6 +20,7 @@
 // sums them in split order and runs the epilogue -- deterministic, and no CTA ever waits on
 // another.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "fmoe_internal.h"
 #include "fmoe_ptx.cuh"
@@ -38,7 +39,8 @@ struct GemmArgs {
   uint8_t* h_hi;
   uint8_t* h_lo;
   float* h_scale_t;        // [I/128][cap]
-  __nv_bfloat16* y;        // [cap][H]
+  __half* y;               // [cap][H] fp16, scaled by y_scale
+  float* y_scale;          // [cap][H/256] power-of-two scale per slot per n-tile
   int E, H, I;
   int64_t cap;
   int partial_rows;
@@ -74,8 +76,6 @@ struct GemmTail {
   int last_flag;
   int abort_flag;
   int pad_;
-  float sb0[64];
-  float sb1[64];
   float amax_x[2][128];
   int ebase[kMaxLocalExperts + 1];
   int ecnt[kMaxLocalExperts];
@@ -285,27 +285,40 @@ __global__ void __launch_bounds__(kThreads, 1)
     float acc[128];
     for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
       const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
+      // every epilogue thread has finished the previous unit's shared-memory exchanges
       named_bar_sync(1, kEpiWarps * 32);
-      for (int i = etid; i < nkb; i += kEpiWarps * 32) {
-        if (KIND == 1) {
-          const int nb1 = args.I / kBlock;
-          const size_t base = static_cast<size_t>(u.e) * 2 * nb1;
-          tail->sb0[i] = __ldg(args.w_scale + (base + u.n) * nkb + i);
-          tail->sb1[i] = __ldg(args.w_scale + (base + nb1 + u.n) * nkb + i);
-        } else {
-          const size_t base = static_cast<size_t>(u.e) * (args.H / kBlock);
-          tail->sb0[i] = __ldg(args.w_scale + (base + 2 * u.n) * nkb + i);
-          tail->sb1[i] = __ldg(args.w_scale + (base + 2 * u.n + 1) * nkb + i);
-        }
+      // weight-scale rows of this tile's two 128-row halves (gate/up, or two n-blocks)
+      const float* sb0_ptr;
+      const float* sb1_ptr;
+      if (KIND == 1) {
+        const int nb1 = args.I / kBlock;
+        const size_t base = static_cast<size_t>(u.e) * 2 * nb1;
+        sb0_ptr = args.w_scale + (base + u.n) * nkb;
+        sb1_ptr = args.w_scale + (base + nb1 + u.n) * nkb;
+      } else {
+        const size_t base = static_cast<size_t>(u.e) * (args.H / kBlock);
+        sb0_ptr = args.w_scale + (base + 2 * u.n) * nkb;
+        sb1_ptr = args.w_scale + (base + 2 * u.n + 1) * nkb;
       }
-      named_bar_sync(1, kEpiWarps * 32);
+      // Warps whose 32 rows are all padding skip the TMEM reads (their rows are discarded);
+      // they still wait for each buffer before releasing it, which keeps the phases aligned.
+      const bool warp_rows = q * 32 < u.nrows;
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
       const float* sa_ptr = args.a_scale_t + u.row0 + r;
-      float sa_next = u.kb0 < u.kb1 ? __ldg(sa_ptr + static_cast<int64_t>(u.kb0) * cap) : 0.0f;
+      float sa_next = 0.0f, sb0_next = 0.0f, sb1_next = 0.0f;
+      if (u.kb0 < u.kb1) {
+        sa_next = __ldg(sa_ptr + static_cast<int64_t>(u.kb0) * cap);
+        sb0_next = __ldg(sb0_ptr + u.kb0);
+        sb1_next = __ldg(sb1_ptr + u.kb0);
+      }
       for (int kb = u.kb0; kb < u.kb1; ++kb, ++kt) {
-        const float sa = sa_next;
-        if (kb + 1 < u.kb1) sa_next = __ldg(sa_ptr + static_cast<int64_t>(kb + 1) * cap);
+        const float sa = sa_next, sb0 = sb0_next, sb1 = sb1_next;
+        if (kb + 1 < u.kb1) {
+          sa_next = __ldg(sa_ptr + static_cast<int64_t>(kb + 1) * cap);
+          sb0_next = __ldg(sb0_ptr + kb + 1);
+          sb1_next = __ldg(sb1_ptr + kb + 1);
+        }
         const int b = kt & 1;
         const int rb = kt >> 1;
         bool got = ok && wait_or_abort(&tail->tfull[b], rb & 1, abort_flag);
@@ -314,20 +327,32 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) raise_abort(tail, args.status, kErr);
           ok = false;
         }
-        if (got) {
+        if (got && warp_rows) {
           tc_fence_after();
-          const float f0 = sa * tail->sb0[kb];
-          const float f1 = sa * tail->sb1[kb];
+          const float f0 = sa * sb0;
+          const float f1 = sa * sb1;
           const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kTileN;
+          // 8 chunks of 16 columns: gate (or n-block 0) cols g*64 + [0,64), then up (n-block 1)
+          // cols 128 + g*64 + [0,64). Chunk c+1 is in flight while chunk c is accumulated.
+          float va[16], vb[16];
+          tmem_ld_32x32b_x16(taddr + g * 64, va);
+          tmem_ld_wait16(va);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int col = (c < 2 ? 0 : 128) + g * 64 + (c & 1) * 32;
-            const float f = c < 2 ? f0 : f1;
-            float v[32];
-            tmem_ld_32x32b_x32(taddr + col, v);
-            tmem_ld_wait();
+          for (int c = 0; c < 8; ++c) {
+            const int cn = c + 1;
+            const int coln = (cn < 4 ? 0 : 128) + g * 64 + (cn & 3) * 16;
+            const float f = c < 4 ? f0 : f1;
+            if ((c & 1) == 0) {
+              if (cn < 8) tmem_ld_32x32b_x16(taddr + coln, vb);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(v[i], f, acc[c * 32 + i]);
+              for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(va[i], f, acc[c * 16 + i]);
+              if (cn < 8) tmem_ld_wait16(vb);
+            } else {
+              if (cn < 8) tmem_ld_32x32b_x16(taddr + coln, va);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(vb[i], f, acc[c * 16 + i]);
+              if (cn < 8) tmem_ld_wait16(va);
+            }
           }
           tc_fence_before();
         }
@@ -429,6 +454,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = scale;
       } else {
+        // fp16 rows with one power-of-two scale per slot per 256 columns: the smallest 2^k
+        // with amax / 2^k <= 16384, so the fp16 range is never exceeded and the scaling is
+        // exact; relative precision stays 2^-11.
+        float amax = 0.0f;
+        if (valid) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) amax = fmaxf(amax, fabsf(acc[c]));
+        }
+        tail->amax_x[g][r] = amax;
+        named_bar_sync(1, kEpiWarps * 32);
+        amax = fmaxf(tail->amax_x[0][r], tail->amax_x[1][r]);
+        int ex = 0;
+        const float m = frexpf(amax, &ex);          // amax = m * 2^ex, m in [0.5, 1)
+        const int k = (m > 0.5f ? ex : ex - 1) - 14;  // ceil(log2(amax)) - 14
+        const float inv = ldexpf(1.0f, -k);
         if (valid) {
           const size_t row = static_cast<size_t>(u.row0) + r;
 #pragma unroll
@@ -440,13 +480,14 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint32_t wv[4];
 #pragma unroll
               for (int w = 0; w < 4; ++w) {
-                const __nv_bfloat162 pr = __floats2bfloat162_rn(acc[h * 64 + v8 * 8 + 2 * w],
-                                                                acc[h * 64 + v8 * 8 + 2 * w + 1]);
+                const __half2 pr = __floats2half2_rn(acc[h * 64 + v8 * 8 + 2 * w] * inv,
+                                                     acc[h * 64 + v8 * 8 + 2 * w + 1] * inv);
                 wv[w] = *reinterpret_cast<const uint32_t*>(&pr);
               }
               dst[v8] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
             }
           }
+          if (g == 0) args.y_scale[row * (args.H / kTileN) + u.n] = ldexpf(1.0f, k);
         }
       }
     }
@@ -489,7 +530,8 @@ static cudaError_t launch_gemm_kind(const RunParams& p, const CUtensorMap& a0,
   a.h_hi = ws + L.h_hi;
   a.h_lo = ws + L.h_lo;
   a.h_scale_t = reinterpret_cast<float*>(ws + L.h_scale_t);
-  a.y = reinterpret_cast<__nv_bfloat16*>(ws + L.y_rows);
+  a.y = reinterpret_cast<__half*>(ws + L.y_rows);
+  a.y_scale = reinterpret_cast<float*>(ws + L.y_scale);
   a.E = p.E;
   a.H = p.H;
   a.I = p.I;

@@ -40,11 +40,22 @@ enum PlanWord {
 struct Layout {
   size_t total;
   size_t status, plan, topk_ids, topk_w, expert_count, expert_base, slot_token, slot_weight;
-  size_t token_slot, token_weight, a_perm, a_scale_t, h_hi, h_lo, h_scale_t, y_rows;
-  size_t partials, counters;
+  size_t token_slot, token_weight, a_perm, a_scale_t, h_hi, h_lo, h_scale_t, y_rows, y_scale;
+  size_t partials, counters, block_hist, block_off;
   int64_t cap;          // padded slot capacity
   int64_t partial_rows; // rows stored per split-K partial tile (<= 128)
+  int tpb;              // tokens per routing block
+  int nblocks;          // routing blocks = ceil(T / tpb)
 };
+
+// Tokens per routing block: the scan kernel keeps one count per (block, local expert) in
+// shared memory, at most kMaxBlockCounts of them.
+constexpr int kMaxBlockCounts = 8192;
+__host__ __device__ inline int routing_tpb(int T, int E) {
+  int tpb = 8;
+  while (static_cast<long>((T + tpb - 1) / tpb) * E > kMaxBlockCounts && tpb < (1 << 20)) tpb *= 2;
+  return tpb;
+}
 
 // Host + device: compute the workspace layout.
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -78,8 +89,13 @@ __host__ __device__ inline Layout make_layout(int T, int E, int H, int I) {
   L.h_lo = take((size_t)L.cap * I);
   L.h_scale_t = take((size_t)(I / kBlock) * L.cap * 4);
   L.y_rows = take((size_t)L.cap * H * 2);
+  L.y_scale = take((size_t)L.cap * (H / kTileN) * 4);
   L.partials = take((size_t)kMaxSplitUnits * L.partial_rows * kTileN * 4);
   L.counters = take((size_t)2 * kMaxSplitUnits * 4);
+  L.tpb = routing_tpb(T, E);
+  L.nblocks = T > 0 ? (T + L.tpb - 1) / L.tpb : 0;
+  L.block_hist = take((size_t)(L.nblocks > 0 ? L.nblocks : 1) * E * 4);
+  L.block_off = take((size_t)(L.nblocks > 0 ? L.nblocks : 1) * E * 4);
   L.total = o;
   return L;
 }
@@ -106,8 +122,10 @@ struct RunParams {
 // Launchers (fmoe_kernels.cu / fmoe_gemm.cu). Return cudaGetLastError() of the launch.
 cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias, int bias_dtype,
                          int T, float rsf, int32_t* topk_ids, float* topk_w, cudaStream_t s);
-cudaError_t launch_plan(const RunParams& p, cudaStream_t s);
-cudaError_t launch_gather(const RunParams& p, cudaStream_t s);
+// routing + per-block local-expert histogram -> scan -> scatter + activation gather
+cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s);
+cudaError_t launch_scan(const RunParams& p, cudaStream_t s);
+cudaError_t launch_scatter_gather(const RunParams& p, cudaStream_t s);
 cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUtensorMap& tm_w1,
                          cudaStream_t s);
 cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,

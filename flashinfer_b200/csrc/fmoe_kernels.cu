@@ -8,6 +8,7 @@
 //   k_gather   <- index_select of rows and scales    kernel.py:699-703
 //   k_combine  <- _weighted_scatter_add_kernel       kernel.py:337-368 + bf16 cast :820-823
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <math.h>
 
 #include "fmoe_internal.h"
@@ -47,6 +48,112 @@ __device__ __forceinline__ float sigmoid_rn(float x) {
   return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
 }
 
+// Routes one token with one warp. Returns, in every lane, the 8 picks (selection order:
+// descending biased score, lowest index first on ties) and their weights.
+template <typename TL>
+__device__ __forceinline__ void route_token(const TL* __restrict__ row, const float (&b)[8],
+                                            float rsf, int lane, int (&ids)[kTopK],
+                                            float (&wts)[kTopK]) {
+  const float NEG_INF = -INFINITY;
+  float x[8], s[8], sb[8];
+  load8<TL>(row + lane * 8, x);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    s[i] = sigmoid_rn(x[i]);
+    sb[i] = __fadd_rn(s[i], b[i]);
+  }
+  // Top-2 of the biased scores in each group of 32 (kernel.py:406-416).
+  float m1 = NEG_INF, m2 = NEG_INF;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float v = sb[i];
+    if (v > m1) {
+      m2 = m1;
+      m1 = v;
+    } else if (v > m2) {
+      m2 = v;
+    }
+  }
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    const float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
+    const float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
+    const float n1 = fmaxf(m1, o1);
+    const float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
+    m1 = n1;
+    m2 = n2;
+  }
+  const float gscore = __fadd_rn(m1, m2);
+  float gs[kGroups];
+#pragma unroll
+  for (int g = 0; g < kGroups; ++g) gs[g] = __shfl_sync(0xffffffffu, gscore, 4 * g);
+  // Keep the 4 best groups; ties go to the lower group index (kernel.py:418-426).
+  uint32_t gmask = 0;
+#pragma unroll
+  for (int g = 0; g < kGroups; ++g) {
+    int rank = 0;
+#pragma unroll
+    for (int h = 0; h < kGroups; ++h) rank += (gs[h] > gs[g]) || (gs[h] == gs[g] && h < g);
+    if (rank < kTopKGroups) gmask |= 1u << g;
+  }
+  const bool kept = (gmask >> (lane >> 2)) & 1u;
+  // Top-8 over the kept groups by biased score; ties to the lowest index (kernel.py:428-438).
+  // Each candidate becomes an order-preserving 32-bit key, so one warp-wide max reduction
+  // (redux.sync) finds the best score and a second one the lowest index holding it.
+  uint32_t key[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint32_t u = __float_as_uint(sb[i] + 0.0f);  // -0 -> +0
+    key[i] = kept ? ((u & 0x80000000u) ? ~u : (u | 0x80000000u)) : 0u;
+  }
+  float sv[kTopK];
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) {
+    uint32_t best = 0;
+    int bi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (key[i] > best) {  // strict '>' keeps the lowest local index among equal keys
+        best = key[i];
+        bi = i;
+      }
+    }
+    const uint32_t top = __reduce_max_sync(0xffffffffu, best);
+    const uint32_t mine = (best == top) ? static_cast<uint32_t>(255 - (lane * 8 + bi)) : 0u;
+    const int win = 255 - static_cast<int>(__reduce_max_sync(0xffffffffu, mine));
+    const int wl = win >> 3, wi = win & 7;
+    float s_win = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i == wi) s_win = s[i];
+    sv[k] = __shfl_sync(0xffffffffu, s_win, wl);
+    ids[k] = win;
+    if (lane == wl) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i == wi) key[i] = 0u;
+    }
+  }
+  // Weights from the un-biased scores (moe.py:165-168): (s / (sum + 1e-20)) * rsf, with the
+  // sum taken in selection order.
+  float denom = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) denom = __fadd_rn(denom, sv[k]);
+  denom = __fadd_rn(denom, 1e-20f);
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) wts[k] = __fmul_rn(__fdiv_rn(sv[k], denom), rsf);
+}
+
+__device__ __forceinline__ void store_picks(int32_t* ids_out, float* w_out, int t,
+                                            const int (&ids)[kTopK], const float (&w)[kTopK]) {
+  int4* io = reinterpret_cast<int4*>(ids_out + static_cast<size_t>(t) * kTopK);
+  float4* wo = reinterpret_cast<float4*>(w_out + static_cast<size_t>(t) * kTopK);
+  io[0] = make_int4(ids[0], ids[1], ids[2], ids[3]);
+  io[1] = make_int4(ids[4], ids[5], ids[6], ids[7]);
+  wo[0] = make_float4(w[0], w[1], w[2], w[3]);
+  wo[1] = make_float4(w[4], w[5], w[6], w[7]);
+}
+
 template <typename TL, typename TB>
 __global__ void __launch_bounds__(256) k_route(const TL* __restrict__ logits,
                                                const TB* __restrict__ bias, int T, float rsf,
@@ -57,104 +164,48 @@ __global__ void __launch_bounds__(256) k_route(const TL* __restrict__ logits,
   const int nwarps = gridDim.x * (blockDim.x >> 5);
   float b[8];
   load8<TB>(bias + lane * 8, b);
-  const float NEG_INF = -INFINITY;
-
   for (int t = warp0; t < T; t += nwarps) {
-    float x[8], s[8], sb[8];
-    load8<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal + lane * 8, x);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      s[i] = sigmoid_rn(x[i]);
-      sb[i] = __fadd_rn(s[i], b[i]);
-    }
-    // Top-2 of the biased scores in each group of 32 (kernel.py:406-416).
-    float m1 = NEG_INF, m2 = NEG_INF;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float v = sb[i];
-      if (v > m1) {
-        m2 = m1;
-        m1 = v;
-      } else if (v > m2) {
-        m2 = v;
-      }
-    }
-#pragma unroll
-    for (int off = 1; off <= 2; off <<= 1) {
-      const float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
-      const float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
-      const float n1 = fmaxf(m1, o1);
-      const float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
-      m1 = n1;
-      m2 = n2;
-    }
-    const float gscore = __fadd_rn(m1, m2);
-    float gs[kGroups];
-#pragma unroll
-    for (int g = 0; g < kGroups; ++g) gs[g] = __shfl_sync(0xffffffffu, gscore, 4 * g);
-    // Keep the 4 best groups; ties go to the lower group index (kernel.py:418-426).
-    uint32_t gmask = 0;
-#pragma unroll
-    for (int g = 0; g < kGroups; ++g) {
-      int rank = 0;
-#pragma unroll
-      for (int h = 0; h < kGroups; ++h)
-        rank += (gs[h] > gs[g]) || (gs[h] == gs[g] && h < g);
-      if (rank < kTopKGroups) gmask |= 1u << g;
-    }
-    const bool kept = (gmask >> (lane >> 2)) & 1u;
-    // Top-8 over the kept groups by biased score; ties to the lowest index (kernel.py:428-438).
-    uint32_t taken = kept ? 0u : 0xffu;
     int ids[kTopK];
-    float sv[kTopK];
+    float w[kTopK];
+    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, lane, ids, w);
+    if (lane == 0) store_picks(ids_out, w_out, t, ids, w);
+  }
+}
+
+// Routing fused with the per-block local-expert histogram. Block b owns tokens
+// [b*tpb, min(T, (b+1)*tpb)); the histogram is order-free (shared-memory atomics on counts).
+template <typename TL, typename TB>
+__global__ void __launch_bounds__(256) k_route_hist(const TL* __restrict__ logits,
+                                                    const TB* __restrict__ bias, int T, int tpb,
+                                                    float rsf, int local_start, int E,
+                                                    int32_t* __restrict__ ids_out,
+                                                    float* __restrict__ w_out,
+                                                    int32_t* __restrict__ block_hist) {
+  __shared__ int hist[kMaxLocalExperts];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  float b[8];
+  load8<TB>(bias + lane * 8, b);
+  const int t0 = blockIdx.x * tpb;
+  const int t1 = min(T, t0 + tpb);
+  for (int t = t0 + warp; t < t1; t += blockDim.x >> 5) {
+    int ids[kTopK];
+    float w[kTopK];
+    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, lane, ids, w);
+    if (lane == 0) store_picks(ids_out, w_out, t, ids, w);
+    if (lane < kTopK) {
+      int mine = ids[0];
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-      float bv = NEG_INF, bs = 0.0f;
-      int bi = 0x7fffffff;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        // strict '>' keeps the lowest index among equal scores
-        if (!((taken >> i) & 1u) && (bi == 0x7fffffff || sb[i] > bv)) {
-          bv = sb[i];
-          bs = s[i];
-          bi = lane * 8 + i;
-        }
-      }
-#pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        const float os = __shfl_xor_sync(0xffffffffu, bs, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-        const bool better = (oi != 0x7fffffff) &&
-                            (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi));
-        if (better) {
-          bv = ov;
-          bs = os;
-          bi = oi;
-        }
-      }
-      ids[k] = bi;
-      sv[k] = bs;
-      if ((bi >> 3) == lane) taken |= 1u << (bi & 7);
-    }
-    // Weights from the un-biased scores (moe.py:165-168): (s / (sum + 1e-20)) * rsf, with the
-    // sum taken in selection order.
-    float denom = 0.0f;
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) denom = __fadd_rn(denom, sv[k]);
-    denom = __fadd_rn(denom, 1e-20f);
-    if (lane == 0) {
-      int4* io = reinterpret_cast<int4*>(ids_out + static_cast<size_t>(t) * kTopK);
-      float4* wo = reinterpret_cast<float4*>(w_out + static_cast<size_t>(t) * kTopK);
-      float w[kTopK];
-#pragma unroll
-      for (int k = 0; k < kTopK; ++k) w[k] = __fmul_rn(__fdiv_rn(sv[k], denom), rsf);
-      io[0] = make_int4(ids[0], ids[1], ids[2], ids[3]);
-      io[1] = make_int4(ids[4], ids[5], ids[6], ids[7]);
-      wo[0] = make_float4(w[0], w[1], w[2], w[3]);
-      wo[1] = make_float4(w[4], w[5], w[6], w[7]);
+      for (int k = 1; k < kTopK; ++k)
+        if (lane == k) mine = ids[k];
+      const int le = mine - local_start;
+      if (le >= 0 && le < E) atomicAdd(&hist[le], 1);
     }
   }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    block_hist[static_cast<size_t>(blockIdx.x) * E + e] = hist[e];
 }
 
 cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias, int bias_dtype,
@@ -184,21 +235,25 @@ cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias,
 }
 
 // ------------------------------------------------------------------------------------------
-// Plan: one CTA of 1024 threads builds the deterministic, stable permutation.
-//   pass 1: per-expert counts (order-free shared-memory atomics) -> padded bases
-//   pass 2: chunks of 1024 tokens; per-warp ballots give each (token, expert) its rank among
-//           earlier tokens, so slots are ascending in token id within each expert
-//   pass 3: padding slots, split-K choice, counter reset
+// Permutation plan, deterministic and stable (tokens ascending within each expert).
+//   k_route_hist  per routing block: how many of its tokens pick each local expert
+//   k_scan        one CTA: exclusive scan over blocks per expert, padded expert bases, the
+//                 GEMM work plan (tiles, K splits), counter and status reset
+//   k_scatter     per routing block: rank of each (token, expert) among the block's earlier
+//                 tokens (warp ballots), slot = block offset + rank; then the block copies the
+//                 e4m3 rows and 128-column scales of its picks into the permuted buffers and
+//                 zero-fills the padding slots it owns.
 // ------------------------------------------------------------------------------------------
 __device__ int choose_split(int tiles, int nkb, int G) {
   if (tiles <= 0 || tiles >= G) return 1;
   int best = 1;
   long best_cost = 0x7fffffffffffL;
   for (int s = 1; s <= kMaxSplit && s <= nkb; ++s) {
-    if (static_cast<long>(tiles) * s > kMaxSplitUnits) break;
+    if (s > 1 && static_cast<long>(tiles) * s > kMaxSplitUnits) break;
     const long waves = (static_cast<long>(tiles) * s + G - 1) / G;
     const long per = (nkb + s - 1) / s;
-    const long cost = waves * per + (s > 1 ? 1 : 0);
+    // a split adds one partial-tile round trip, about one K block of work
+    const long cost = waves * per + (s > 1 ? waves : 0);
     if (cost < best_cost) {
       best_cost = cost;
       best = s;
@@ -207,49 +262,47 @@ __device__ int choose_split(int tiles, int nkb, int G) {
   return best;
 }
 
-struct PlanSmem {
-  int cnt[kMaxLocalExperts];
-  int base[kMaxLocalExperts + 1];
-  int run[kMaxLocalExperts];
-  int wcnt[32][kMaxLocalExperts];
-};
-
-__global__ void __launch_bounds__(1024) k_plan(const int32_t* __restrict__ ids,
-                                               const float* __restrict__ wts, int T,
-                                               int local_start, int E, int H, int I, int G,
-                                               int64_t cap, int32_t* __restrict__ plan,
+__global__ void __launch_bounds__(1024) k_scan(const int32_t* __restrict__ block_hist,
+                                               int nblocks, int E, int H, int I, int G,
+                                               int32_t* __restrict__ block_off,
+                                               int32_t* __restrict__ plan,
                                                int32_t* __restrict__ expert_count,
                                                int32_t* __restrict__ expert_base,
-                                               int32_t* __restrict__ slot_token,
-                                               float* __restrict__ slot_weight,
-                                               int32_t* __restrict__ token_slot,
-                                               float* __restrict__ token_weight,
                                                int32_t* __restrict__ counters,
                                                int32_t* __restrict__ status) {
-  __shared__ PlanSmem sm;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  for (int e = tid; e < E; e += blockDim.x) {
-    sm.cnt[e] = 0;
-    sm.run[e] = 0;
-  }
+  __shared__ int sh[kMaxBlockCounts];
+  __shared__ int cnt[kMaxLocalExperts];
+  __shared__ int base[kMaxLocalExperts + 1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+  const int n = nblocks * E;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sh[i] = block_hist[i];
   __syncthreads();
-  // pass 1: counts
-  for (int t = tid; t < T; t += blockDim.x) {
+  // warp w scans experts w, w+32, ...: exclusive prefix over blocks, 32 blocks per step
+  for (int e = warp; e < E; e += nwarp) {
+    int run = 0;
+    for (int b0 = 0; b0 < nblocks; b0 += 32) {
+      const int b = b0 + lane;
+      const int v = b < nblocks ? sh[b * E + e] : 0;
+      int inc = v;
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-      const int le = ids[static_cast<size_t>(t) * kTopK + k] - local_start;
-      if (le >= 0 && le < E) atomicAdd(&sm.cnt[le], 1);
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += o;
+      }
+      if (b < nblocks) sh[b * E + e] = run + inc - v;
+      run += __shfl_sync(0xffffffffu, inc, 31);
     }
+    if (lane == 0) cnt[e] = run;
   }
   __syncthreads();
-  if (tid == 0) {
+  if (threadIdx.x == 0) {
     int acc = 0, pairs = 0;
     for (int e = 0; e < E; ++e) {
-      sm.base[e] = acc;
-      acc += (sm.cnt[e] + kTileM - 1) / kTileM * kTileM;
-      pairs += sm.cnt[e];
+      base[e] = acc;
+      acc += (cnt[e] + kTileM - 1) / kTileM * kTileM;
+      pairs += cnt[e];
     }
-    sm.base[E] = acc;
+    base[E] = acc;
     const int mtiles = acc / kTileM;
     const int tiles1 = mtiles * (I / kBlock);
     const int tiles2 = mtiles * (H / kTileN);
@@ -267,28 +320,45 @@ __global__ void __launch_bounds__(1024) k_plan(const int32_t* __restrict__ ids,
     status[0] = 0;
   }
   __syncthreads();
-  for (int e = tid; e < E; e += blockDim.x) {
-    expert_count[e] = sm.cnt[e];
-    expert_base[e] = sm.base[e];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    expert_count[e] = cnt[e];
+    expert_base[e] = base[e];
   }
-  if (tid == 0) expert_base[E] = sm.base[E];
-  for (int i = tid; i < 2 * kMaxSplitUnits; i += blockDim.x) counters[i] = 0;
+  if (threadIdx.x == 0) expert_base[E] = base[E];
+  for (int i = threadIdx.x; i < n; i += blockDim.x) block_off[i] = base[i % E] + sh[i];
+  for (int i = threadIdx.x; i < 2 * kMaxSplitUnits; i += blockDim.x) counters[i] = 0;
+}
 
-  // pass 2: stable slots
+struct ScatterSmem {
+  int wcnt[8][kMaxLocalExperts];  // per-warp counts, then per-warp exclusive offsets
+  int run[kMaxLocalExperts];      // slots already handed out per expert in this block
+};
+
+__global__ void __launch_bounds__(256) k_scatter(
+    const int32_t* __restrict__ ids, const float* __restrict__ wts, int T, int tpb,
+    int local_start, int E, const int32_t* __restrict__ block_off,
+    const int32_t* __restrict__ expert_count, const int32_t* __restrict__ expert_base,
+    int32_t* __restrict__ slot_token, float* __restrict__ slot_weight,
+    int32_t* __restrict__ token_slot, float* __restrict__ token_weight) {
+  __shared__ ScatterSmem sm;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int b = blockIdx.x;
+  const int t_begin = b * tpb;
+  const int t_end = min(T, t_begin + tpb);
+  for (int e = tid; e < E; e += blockDim.x) sm.run[e] = block_off[static_cast<size_t>(b) * E + e];
   const int nwords = (E + 31) >> 5;
-  for (int c0 = 0; c0 < T; c0 += blockDim.x) {
+  for (int c0 = t_begin; c0 < t_end; c0 += blockDim.x) {
     const int t = c0 + tid;
     int le[kTopK];
     float lw[kTopK];
     int nloc = 0;
-    if (t < T) {
+    if (t < t_end) {
 #pragma unroll
       for (int k = 0; k < kTopK; ++k) {
         const int e = ids[static_cast<size_t>(t) * kTopK + k] - local_start;
         if (e >= 0 && e < E) {
-          // insertion into the ascending list le[0..nloc)
-          int j = nloc;
           const float w = wts[static_cast<size_t>(t) * kTopK + k];
+          int j = nloc;  // insertion into the ascending list le[0..nloc)
           while (j > 0 && le[j - 1] > e) {
             le[j] = le[j - 1];
             lw[j] = lw[j - 1];
@@ -313,17 +383,14 @@ __global__ void __launch_bounds__(1024) k_plan(const int32_t* __restrict__ ids,
           const bool has = (m >> bit) & 1u;
           const uint32_t bal = __ballot_sync(0xffffffffu, has);
           if (lane == 0) sm.wcnt[warp][ebase + bit] = __popc(bal);
-          if (has) {
-            rank[jp] = __popc(bal & ((1u << lane) - 1u));
-            ++jp;
-          }
+          if (has) rank[jp++] = __popc(bal & ((1u << lane) - 1u));
         }
       }
     }
     __syncthreads();
     for (int e = tid; e < E; e += blockDim.x) {
       int acc = sm.run[e];
-      for (int w = 0; w < 32; ++w) {
+      for (int w = 0; w < 8; ++w) {
         const int c = sm.wcnt[w][e];
         sm.wcnt[w][e] = acc;
         acc += c;
@@ -331,13 +398,12 @@ __global__ void __launch_bounds__(1024) k_plan(const int32_t* __restrict__ ids,
       sm.run[e] = acc;
     }
     __syncthreads();
-    if (t < T) {
+    if (t < t_end) {
       int* ts = token_slot + static_cast<size_t>(t) * kTopK;
       float* tw = token_weight + static_cast<size_t>(t) * kTopK;
       for (int j = 0; j < kTopK; ++j) {
         if (j < nloc) {
-          const int e = le[j];
-          const int slot = sm.base[e] + sm.wcnt[warp][e] + rank[j];
+          const int slot = sm.wcnt[warp][le[j]] + rank[j];
           slot_token[slot] = t;
           slot_weight[slot] = lw[j];
           ts[j] = slot;
@@ -350,10 +416,13 @@ __global__ void __launch_bounds__(1024) k_plan(const int32_t* __restrict__ ids,
     }
     __syncthreads();
   }
-  // pass 3: padding slots
-  for (int e = 0; e < E; ++e) {
-    const int first = sm.base[e] + sm.cnt[e];
-    const int end = sm.base[e + 1];
+  // Padding slots of the experts this block owns (expert e -> block e mod nblocks) are marked
+  // empty. Their activation rows are never initialised: a padding row of the A tile only feeds
+  // the same row of the accumulator, which the epilogue replaces with zeros.
+  const int nblocks = gridDim.x;
+  for (int e = b; e < E; e += nblocks) {
+    const int first = expert_base[e] + expert_count[e];
+    const int end = expert_base[e + 1];
     for (int s = first + tid; s < end; s += blockDim.x) {
       slot_token[s] = -1;
       slot_weight[s] = 0.0f;
@@ -361,79 +430,116 @@ __global__ void __launch_bounds__(1024) k_plan(const int32_t* __restrict__ ids,
   }
 }
 
-cudaError_t launch_plan(const RunParams& p, cudaStream_t s) {
-  uint8_t* ws = p.ws;
-  const Layout& L = p.L;
-  k_plan<<<1, 1024, 0, s>>>(
-      reinterpret_cast<const int32_t*>(ws + L.topk_ids),
-      reinterpret_cast<const float*>(ws + L.topk_w), p.T, p.local_start, p.E, p.H, p.I,
-      p.num_sms, L.cap, reinterpret_cast<int32_t*>(ws + L.plan),
-      reinterpret_cast<int32_t*>(ws + L.expert_count),
-      reinterpret_cast<int32_t*>(ws + L.expert_base),
-      reinterpret_cast<int32_t*>(ws + L.slot_token), reinterpret_cast<float*>(ws + L.slot_weight),
-      reinterpret_cast<int32_t*>(ws + L.token_slot),
-      reinterpret_cast<float*>(ws + L.token_weight), reinterpret_cast<int32_t*>(ws + L.counters),
-      reinterpret_cast<int32_t*>(ws + L.status));
-  return cudaGetLastError();
-}
-
-// ------------------------------------------------------------------------------------------
-// Gather: one warp per slot copies the token's e4m3 row and transposes its 128-column scales
-// into the [H/128, cap] layout the GEMM1 epilogue reads. Padding slots get zeros.
-// ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_gather(const int32_t* __restrict__ plan,
-                                                const int32_t* __restrict__ slot_token,
-                                                const uint8_t* __restrict__ hidden,
-                                                const float* __restrict__ hidden_scale, int T,
-                                                int H, int64_t cap, uint8_t* __restrict__ a_perm,
-                                                float* __restrict__ a_scale_t) {
+// Gather: one warp per token reads the token's e4m3 row once (7168 B = 14 x 16 B per lane)
+// and writes it, with its 128-column scales, to each of the token's slots.
+__global__ void __launch_bounds__(256) k_gather_tokens(const int32_t* __restrict__ token_slot,
+                                                       const uint8_t* __restrict__ hidden,
+                                                       const float* __restrict__ hidden_scale,
+                                                       int T, int H, int64_t cap,
+                                                       uint8_t* __restrict__ a_perm,
+                                                       float* __restrict__ a_scale_t) {
+  constexpr int kMaxVec = 16;  // H <= 8192 (at most 64 scale blocks; 16 B per lane per step)
   const int lane = threadIdx.x & 31;
   const int warp0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nwarps = gridDim.x * (blockDim.x >> 5);
-  const int padded = plan[kPlanPadded];
   const int nvec = H / 16;
   const int nkb = H / kBlock;
-  for (int slot = warp0; slot < padded; slot += nwarps) {
-    const int tok = slot_token[slot];
-    uint4* dst = reinterpret_cast<uint4*>(a_perm + static_cast<size_t>(slot) * H);
-    if (tok >= 0) {
-      const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(tok) * H);
-      for (int i = lane; i < nvec; i += 32) dst[i] = __ldg(src + i);
-      for (int kb = lane; kb < nkb; kb += 32)
-        a_scale_t[static_cast<size_t>(kb) * cap + slot] =
-            __ldg(hidden_scale + static_cast<size_t>(kb) * T + tok);
-    } else {
-      const uint4 z = make_uint4(0, 0, 0, 0);
-      for (int i = lane; i < nvec; i += 32) dst[i] = z;
-      for (int kb = lane; kb < nkb; kb += 32) a_scale_t[static_cast<size_t>(kb) * cap + slot] = 0.f;
+  for (int t = warp0; t < T; t += nwarps) {
+    const int my_slot = lane < kTopK ? __ldg(token_slot + static_cast<size_t>(t) * kTopK + lane) : -1;
+    const int nloc = __popc(__ballot_sync(0xffffffffu, my_slot >= 0));
+    if (nloc == 0) continue;
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(t) * H);
+    uint4 row[kMaxVec];
+#pragma unroll
+    for (int i = 0; i < kMaxVec; ++i)
+      if (lane + 32 * i < nvec) row[i] = __ldg(src + lane + 32 * i);
+    const float sc0 = lane < nkb ? __ldg(hidden_scale + static_cast<size_t>(lane) * T + t) : 0.f;
+    const float sc1 =
+        lane + 32 < nkb ? __ldg(hidden_scale + static_cast<size_t>(lane + 32) * T + t) : 0.f;
+    for (int j = 0; j < nloc; ++j) {
+      const int slot = __shfl_sync(0xffffffffu, my_slot, j);
+      uint4* dst = reinterpret_cast<uint4*>(a_perm + static_cast<size_t>(slot) * H);
+#pragma unroll
+      for (int i = 0; i < kMaxVec; ++i)
+        if (lane + 32 * i < nvec) dst[lane + 32 * i] = row[i];
+      if (lane < nkb) a_scale_t[static_cast<size_t>(lane) * cap + slot] = sc0;
+      if (lane + 32 < nkb) a_scale_t[static_cast<size_t>(lane + 32) * cap + slot] = sc1;
     }
   }
 }
 
-cudaError_t launch_gather(const RunParams& p, cudaStream_t s) {
+template <typename F>
+static cudaError_t dispatch_dtypes(int ld, int bd, F&& f) {
+  if (ld == FMOE_DTYPE_F32 && bd == FMOE_DTYPE_BF16) return f(float(), __nv_bfloat16());
+  if (ld == FMOE_DTYPE_F32 && bd == FMOE_DTYPE_F32) return f(float(), float());
+  if (ld == FMOE_DTYPE_BF16 && bd == FMOE_DTYPE_BF16) return f(__nv_bfloat16(), __nv_bfloat16());
+  return f(__nv_bfloat16(), float());
+}
+
+cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s) {
+  if (p.T <= 0) return cudaSuccess;
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
-  int blocks = static_cast<int>((L.cap + 7) / 8);
-  const int max_blocks = p.num_sms * 8;
-  if (blocks > max_blocks) blocks = max_blocks;
-  if (blocks < 1) blocks = 1;
-  k_gather<<<blocks, 256, 0, s>>>(
-      reinterpret_cast<const int32_t*>(ws + L.plan),
-      reinterpret_cast<const int32_t*>(ws + L.slot_token), p.hidden, p.hidden_scale, p.T, p.H,
-      L.cap, ws + L.a_perm, reinterpret_cast<float*>(ws + L.a_scale_t));
+  return dispatch_dtypes(p.logits_dtype, p.bias_dtype, [&](auto tl, auto tb) {
+    using TL = decltype(tl);
+    using TB = decltype(tb);
+    k_route_hist<TL, TB><<<L.nblocks, 256, 0, s>>>(
+        static_cast<const TL*>(p.logits), static_cast<const TB*>(p.bias), p.T, L.tpb, p.rsf,
+        p.local_start, p.E, reinterpret_cast<int32_t*>(ws + L.topk_ids),
+        reinterpret_cast<float*>(ws + L.topk_w), reinterpret_cast<int32_t*>(ws + L.block_hist));
+    return cudaGetLastError();
+  });
+}
+
+cudaError_t launch_scan(const RunParams& p, cudaStream_t s) {
+  uint8_t* ws = p.ws;
+  const Layout& L = p.L;
+  k_scan<<<1, 1024, 0, s>>>(reinterpret_cast<const int32_t*>(ws + L.block_hist), L.nblocks, p.E,
+                            p.H, p.I, p.num_sms, reinterpret_cast<int32_t*>(ws + L.block_off),
+                            reinterpret_cast<int32_t*>(ws + L.plan),
+                            reinterpret_cast<int32_t*>(ws + L.expert_count),
+                            reinterpret_cast<int32_t*>(ws + L.expert_base),
+                            reinterpret_cast<int32_t*>(ws + L.counters),
+                            reinterpret_cast<int32_t*>(ws + L.status));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_gather(const RunParams& p, cudaStream_t s) {
+  if (p.T <= 0) return cudaSuccess;
+  uint8_t* ws = p.ws;
+  const Layout& L = p.L;
+  k_scatter<<<L.nblocks, 256, 0, s>>>(
+      reinterpret_cast<const int32_t*>(ws + L.topk_ids),
+      reinterpret_cast<const float*>(ws + L.topk_w), p.T, L.tpb, p.local_start, p.E,
+      reinterpret_cast<const int32_t*>(ws + L.block_off),
+      reinterpret_cast<const int32_t*>(ws + L.expert_count),
+      reinterpret_cast<const int32_t*>(ws + L.expert_base),
+      reinterpret_cast<int32_t*>(ws + L.slot_token), reinterpret_cast<float*>(ws + L.slot_weight),
+      reinterpret_cast<int32_t*>(ws + L.token_slot),
+      reinterpret_cast<float*>(ws + L.token_weight));
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  int blocks = (p.T + 7) / 8;
+  if (blocks > p.num_sms * 8) blocks = p.num_sms * 8;
+  k_gather_tokens<<<blocks, 256, 0, s>>>(reinterpret_cast<const int32_t*>(ws + L.token_slot),
+                                         p.hidden, p.hidden_scale, p.T, p.H, L.cap,
+                                         ws + L.a_perm, reinterpret_cast<float*>(ws + L.a_scale_t));
   return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------------------------------
 // Combine: one CTA per token sums w * Y[slot] over the token's local picks in ascending
 // expert order (the definition's loop order, moe.py:79-98), in registers, then writes bf16.
-// Tokens without local picks get zeros (kernel.py:692-695 zero-fills when nothing is local).
+// Y rows are fp16 with a power-of-two scale per 256 columns (exact to apply). Tokens without
+// local picks get zeros (kernel.py:692-695 zero-fills when nothing is local).
 // ------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) k_combine(const int32_t* __restrict__ token_slot,
                                                  const float* __restrict__ token_weight,
-                                                 const __nv_bfloat16* __restrict__ y, int T,
+                                                 const __half* __restrict__ y,
+                                                 const float* __restrict__ y_scale, int T,
                                                  int H, __nv_bfloat16* __restrict__ out) {
   const int nvec = H / 8;
+  const int ntile = H / kTileN;
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
     int slots[kTopK];
     float w[kTopK];
@@ -443,20 +549,22 @@ __global__ void __launch_bounds__(128) k_combine(const int32_t* __restrict__ tok
       w[j] = __ldg(token_weight + static_cast<size_t>(t) * kTopK + j);
     }
     for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+      const int tile = (v * 8) / kTileN;
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
         if (slots[j] < 0) break;
-        const uint4 raw =
-            __ldg(reinterpret_cast<const uint4*>(y + static_cast<size_t>(slots[j]) * H) + v);
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        const size_t row = static_cast<size_t>(slots[j]);
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(y + row * H) + v);
+        const float f = __ldg(y_scale + row * ntile + tile);
+        const __half2* h = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float2 f = __bfloat1622float2(h[i]);
-          acc[2 * i] = fmaf(w[j], f.x, acc[2 * i]);
-          acc[2 * i + 1] = fmaf(w[j], f.y, acc[2 * i + 1]);
+          const float2 q = __half22float2(h[i]);
+          acc[2 * i] = fmaf(w[j], q.x * f, acc[2 * i]);
+          acc[2 * i + 1] = fmaf(w[j], q.y * f, acc[2 * i + 1]);
         }
       }
       uint4 o;
@@ -475,8 +583,9 @@ cudaError_t launch_combine(const RunParams& p, cudaStream_t s) {
   int blocks = p.T < p.num_sms * 16 ? p.T : p.num_sms * 16;
   k_combine<<<blocks, 128, 0, s>>>(reinterpret_cast<const int32_t*>(ws + L.token_slot),
                                    reinterpret_cast<const float*>(ws + L.token_weight),
-                                   reinterpret_cast<const __nv_bfloat16*>(ws + L.y_rows), p.T,
-                                   p.H, p.output);
+                                   reinterpret_cast<const __half*>(ws + L.y_rows),
+                                   reinterpret_cast<const float*>(ws + L.y_scale), p.T, p.H,
+                                   p.output);
   return cudaGetLastError();
 }
 

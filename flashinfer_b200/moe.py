@@ -232,4 +232,8 @@ class WorkspaceView:
         return hi, lo, sc
 
     def y_rows(self):
-        return self._view(self.lay.y_rows, self.cap * self.H, torch.bfloat16).view(self.cap, self.H)
+        """Per-slot GEMM2 rows decoded to fp32 (fp16 payload times its per-tile scale)."""
+        y = self._view(self.lay.y_rows, self.cap * self.H, torch.float16).view(self.cap, self.H)
+        sc = self._view(self.lay.y_scale, self.cap * (self.H // 256),
+                        torch.float32).view(self.cap, self.H // 256)
+        return y.float() * sc.repeat_interleave(256, dim=1)

@@ -54,8 +54,8 @@ extern "C" {
 
 /* Stop points for staged execution (tests inspect the workspace in between). */
 #define FMOE_STOP_NONE     0
-#define FMOE_STOP_ROUTE    1   /* after routing + permutation plan     */
-#define FMOE_STOP_GATHER   2   /* after the activation row gather      */
+#define FMOE_STOP_ROUTE    1   /* after routing, permutation and the activation gather */
+#define FMOE_STOP_GATHER   2   /* same point (the gather is fused into the permutation) */
 #define FMOE_STOP_GEMM1    3   /* after GEMM1 + SwiGLU (intermediate)  */
 #define FMOE_STOP_GEMM2    4   /* after GEMM2 (per-slot output rows)   */
 
@@ -119,11 +119,16 @@ typedef struct FmoeLayout {
   size_t h_hi;            /* e4m3   [cap, I] SwiGLU output, leading term                       */
   size_t h_lo;            /* e4m3   [cap, I] SwiGLU output, residual term                      */
   size_t h_scale_t;       /* fp32   [I/128, cap]                                               */
-  size_t y_rows;          /* bf16   [cap, H] per-slot GEMM2 output rows                        */
+  size_t y_rows;          /* fp16   [cap, H] per-slot GEMM2 output rows, scaled by y_scale     */
+  size_t y_scale;         /* fp32   [cap, H/256] power-of-two scale per slot per 256 columns   */
   size_t partials;        /* fp32   split-K partial tiles                                      */
   size_t counters;        /* int32  split-K arrival counters                                   */
+  size_t block_hist;      /* int32  [nblocks, E_local] local picks per routing block           */
+  size_t block_off;       /* int32  [nblocks, E_local] first slot of each block per expert     */
   int64_t cap_slots;      /* padded slot capacity                                             */
   int64_t max_units;      /* split-K partial tile capacity                                    */
+  int64_t tokens_per_block; /* tokens per routing block                                       */
+  int64_t num_blocks;     /* routing blocks                                                   */
 } FmoeLayout;
 
 /* Workspace bytes for T tokens and E_local local experts (H, I as in FmoeArgs).

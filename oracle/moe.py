@@ -111,8 +111,23 @@ def quantize_intermediate(h: np.ndarray):
     return hi.reshape(M, N), lo.reshape(M, N), scale
 
 
+def f16_pow2_tiles(y: np.ndarray, tile: int = 256) -> np.ndarray:
+    """fp16 storage of GEMM2 rows with one power-of-two scale per row per 256 columns.
+
+    scale = 2^ceil(log2(amax / 16384)) keeps |y / scale| <= 16384 (fp16 max is 65504).
+    """
+    M, N = y.shape
+    yt = y.reshape(M, N // tile, tile).astype(np.float32)
+    amax = np.abs(yt).max(axis=2)
+    e = np.where(amax > 0, np.ceil(np.log2(np.maximum(amax, 1e-30) / 16384.0)), 0).astype(np.int32)
+    scale = np.ldexp(np.float32(1.0), e).astype(np.float32)
+    q = (yt / scale[:, :, None]).astype(np.float16).astype(np.float32)
+    return (q * scale[:, :, None]).reshape(M, N).astype(np.float32)
+
+
 def moe_device_numerics(hs_raw, hs_scale, w1_raw, s1, w2_raw, s2, ids, weights,
-                        local_start: int, y_bf16: bool = True, two_term: bool = True):
+                        local_start: int, y_bf16: bool = True, two_term: bool = True,
+                        y_format: str = ""):
     """Emulates the CUDA path's arithmetic; returns bf16 bit patterns [T, H]."""
     T, H = hs_raw.shape
     a_all = e4m3_to_f32(hs_raw)
@@ -132,7 +147,9 @@ def moe_device_numerics(hs_raw, hs_scale, w1_raw, s1, w2_raw, s2, ids, weights,
             y = _blockwise_gemm((hi + lo).astype(F32), hsc, w2, s2[le])
         else:
             y = _blockwise_gemm(hi, hsc, w2, s2[le])
-        if y_bf16:
+        if y_format == "f16s":
+            y = f16_pow2_tiles(y)
+        elif y_bf16:
             y = bf16_to_f32(bf16_round(y))
         np.add.at(out, tok, y * w[:, None])
     return bf16_round(out)
