@@ -23,7 +23,9 @@ ERRORS = {
     -6: "FMOE_ERR_DTYPE: unsupported routing logits / bias dtype",
     -7: "FMOE_ERR_CUDA: a CUDA runtime or driver call failed",
     -8: "FMOE_ERR_DEVICE: the current device is not sm_100 (B200)",
+    -9: "FMOE_ERR_NOALLOC_LIMIT: more tokens than fmoe_route_permute_noalloc supports (4096)",
 }
+NOALLOC_MAX_TOKENS = 4096
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
 STOP_NONE, STOP_ROUTE, STOP_GATHER, STOP_GEMM1, STOP_GEMM2 = 0, 1, 2, 3, 4
@@ -31,7 +33,8 @@ STATUS_TIMEOUT_GEMM1 = 0x1
 STATUS_TIMEOUT_GEMM2 = 0x2
 
 EXPORTS = ("fmoe_workspace_size", "fmoe_workspace_layout", "fmoe_run", "fmoe_route",
-           "fmoe_read_status", "fmoe_device_sm_count", "fmoe_version")
+           "fmoe_read_status", "fmoe_device_sm_count", "fmoe_version",
+           "fmoe_route_permute_noalloc")
 
 
 class FmoeArgs(Structure):
@@ -93,6 +96,9 @@ def load() -> ctypes.CDLL:
     lib.fmoe_route.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]
     lib.fmoe_read_status.argtypes = [c_void_p, c_void_p, POINTER(c_int32)]
+    lib.fmoe_route_permute_noalloc.argtypes = [c_void_p, c_int32, c_void_p, c_int32, c_int32,
+                                               c_int32, c_int32, c_float, c_void_p, c_void_p,
+                                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
     lib.fmoe_device_sm_count.argtypes = [POINTER(c_int32)]
     lib.fmoe_version.restype = c_char_p
     for name in EXPORTS:

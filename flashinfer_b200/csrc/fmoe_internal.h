@@ -132,4 +132,28 @@ cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUt
                          const CUtensorMap& tm_w2, cudaStream_t s);
 cudaError_t launch_combine(const RunParams& p, cudaStream_t s);
 
+// Routing + permutation with every buffer passed explicitly (used by the entry point whose
+// scratch lives in a statically allocated device array).
+struct PermuteBuffers {
+  // scratch
+  int32_t* topk_ids;      // [T, 8]
+  float* topk_w;          // [T, 8]
+  int32_t* block_hist;    // [nblocks, E]
+  int32_t* block_off;     // [nblocks, E]
+  int32_t* plan;          // [kPlanWords]
+  int32_t* counters;      // [2 * kMaxSplitUnits]
+  int32_t* status;        // [1]
+  // outputs
+  int32_t* expert_count;  // [E]
+  int32_t* expert_base;   // [E + 1]
+  int32_t* slot_token;    // [cap]
+  float* slot_weight;     // [cap]
+  int32_t* token_slot;    // [T, 8]
+  float* token_weight;    // [T, 8]
+};
+cudaError_t launch_route_permute(const void* logits, int logits_dtype, const void* bias,
+                                 int bias_dtype, int T, int E, int local_start, float rsf,
+                                 int H, int I, int num_sms, const PermuteBuffers& b,
+                                 cudaStream_t s);
+
 }  // namespace fmoe

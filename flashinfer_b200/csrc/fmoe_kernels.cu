@@ -527,6 +527,33 @@ cudaError_t launch_scatter_gather(const RunParams& p, cudaStream_t s) {
   return cudaGetLastError();
 }
 
+cudaError_t launch_route_permute(const void* logits, int logits_dtype, const void* bias,
+                                 int bias_dtype, int T, int E, int local_start, float rsf,
+                                 int H, int I, int num_sms, const PermuteBuffers& bf,
+                                 cudaStream_t s) {
+  if (T <= 0) return cudaSuccess;
+  const int tpb = routing_tpb(T, E);
+  const int nblocks = (T + tpb - 1) / tpb;
+  cudaError_t e = dispatch_dtypes(logits_dtype, bias_dtype, [&](auto tl, auto tb) {
+    using TL = decltype(tl);
+    using TB = decltype(tb);
+    k_route_hist<TL, TB><<<nblocks, 256, 0, s>>>(static_cast<const TL*>(logits),
+                                                  static_cast<const TB*>(bias), T, tpb, rsf,
+                                                  local_start, E, bf.topk_ids, bf.topk_w,
+                                                  bf.block_hist);
+    return cudaGetLastError();
+  });
+  if (e != cudaSuccess) return e;
+  k_scan<<<1, 1024, 0, s>>>(bf.block_hist, nblocks, E, H, I, num_sms, bf.block_off, bf.plan,
+                            bf.expert_count, bf.expert_base, bf.counters, bf.status);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  k_scatter<<<nblocks, 256, 0, s>>>(bf.topk_ids, bf.topk_w, T, tpb, local_start, E,
+                                    bf.block_off, bf.expert_count, bf.expert_base, bf.slot_token,
+                                    bf.slot_weight, bf.token_slot, bf.token_weight);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------------------------------
 // Combine: one CTA per token sums w * Y[slot] over the token's local picks in ascending
 // expert order (the definition's loop order, moe.py:79-98), in registers, then writes bf16.

@@ -43,6 +43,7 @@ extern "C" {
 #define FMOE_ERR_DTYPE        (-6)  /* unsupported routing logits / bias dtype              */
 #define FMOE_ERR_CUDA         (-7)  /* a CUDA runtime or driver call failed                 */
 #define FMOE_ERR_DEVICE       (-8)  /* the current device is not sm_100                     */
+#define FMOE_ERR_NOALLOC_LIMIT (-9) /* more tokens than fmoe_route_permute_noalloc supports  */
 
 /* Device status word bits (fmoe_read_status): set by a kernel whose bounded wait ran out. */
 #define FMOE_STATUS_TIMEOUT_GEMM1  0x1
@@ -153,6 +154,32 @@ FMOE_API int fmoe_route(const void* routing_logits, int32_t logits_dtype, const 
                int32_t bias_dtype, int32_t num_tokens, int32_t num_experts, int32_t top_k,
                int32_t n_group, int32_t topk_group, float routed_scaling_factor,
                int32_t* topk_ids, float* topk_weights, void* cuda_stream);
+
+/* Routing + permutation without any device allocation, for callers that cannot allocate
+ * device memory where they enqueue work (engines that plan every buffer ahead and forbid
+ * allocation at enqueue time, code inside a CUDA graph capture with a fixed memory pool, host
+ * programs bound to the C ABI from runtimes without a device allocator). No counterpart in
+ * the reference, whose run() allocates its temporaries on every call.
+ *
+ * Writes the same tables fmoe_run() builds before its GEMMs: expert_count [E_local],
+ * expert_base [E_local+1] (first slot of each expert, multiples of 128), slot_token and
+ * slot_weight [cap] (cap = cap_slots of fmoe_workspace_layout; padding slots hold -1 / 0),
+ * token_slot and token_weight [T, 8] (a token's local picks in ascending expert order, -1 /
+ * 0 after them). Its scratch is one statically allocated device array of 336,384 bytes,
+ * which every GPU that loads this library keeps until the process exits:
+ *   - num_tokens may be at most 4096; larger requests return FMOE_ERR_NOALLOC_LIMIT;
+ *   - the first call on a device looks up the array's device address (cudaGetSymbolAddress)
+ *     with that device current; make that first call before any stream capture;
+ *   - all calls on a device share the array, so calls whose executions overlap on the GPU
+ *     race and produce undefined tables: order them on one stream. */
+FMOE_API int fmoe_route_permute_noalloc(const void* routing_logits, int32_t logits_dtype,
+                                        const void* routing_bias, int32_t bias_dtype,
+                                        int32_t num_tokens, int32_t num_local_experts,
+                                        int32_t local_expert_offset,
+                                        float routed_scaling_factor, int32_t* expert_count,
+                                        int32_t* expert_base, int32_t* slot_token,
+                                        float* slot_weight, int32_t* token_slot,
+                                        float* token_weight, void* cuda_stream);
 
 /* Copies the device status word into *status (synchronises the stream). Non-zero means a
  * kernel gave up on a bounded wait and its outputs are not valid. */
