@@ -244,16 +244,18 @@ cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias,
 //                 e4m3 rows and 128-column scales of its picks into the permuted buffers and
 //                 zero-fills the padding slots it owns.
 // ------------------------------------------------------------------------------------------
+// K splits per tile for a persistent grid of G CTAs. Cost, in K blocks on the busiest CTA:
+// waves * ceil(nkb / s), plus about two K blocks per unit for the per-unit set-up, and for split
+// units the partial-tile round trip. Ties keep the smaller split.
 __device__ int choose_split(int tiles, int nkb, int G) {
-  if (tiles <= 0 || tiles >= G) return 1;
+  if (tiles <= 0) return 1;
   int best = 1;
   long best_cost = 0x7fffffffffffL;
   for (int s = 1; s <= kMaxSplit && s <= nkb; ++s) {
     if (s > 1 && static_cast<long>(tiles) * s > kMaxSplitUnits) break;
     const long waves = (static_cast<long>(tiles) * s + G - 1) / G;
     const long per = (nkb + s - 1) / s;
-    // a split adds one partial-tile round trip, about one K block of work
-    const long cost = waves * per + (s > 1 ? waves : 0);
+    const long cost = 4 * waves * per + waves * (s > 1 ? 12 : 8);
     if (cost < best_cost) {
       best_cost = cost;
       best = s;
@@ -577,21 +579,31 @@ __global__ void __launch_bounds__(128) k_combine(const int32_t* __restrict__ tok
     }
     for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
       const int tile = (v * 8) / kTileN;
+      // issue every pick's load before reducing (local picks fill slots[0..nloc))
+      uint4 raw[kTopK];
+      float f[kTopK];
+#pragma unroll
+      for (int j = 0; j < kTopK; ++j) {
+        if (slots[j] >= 0) {
+          const size_t row = static_cast<size_t>(slots[j]);
+          raw[j] = __ldg(reinterpret_cast<const uint4*>(y + row * H) + v);
+          f[j] = __ldg(y_scale + row * ntile + tile) * w[j];
+        } else {
+          raw[j] = make_uint4(0, 0, 0, 0);
+          f[j] = 0.0f;
+        }
+      }
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
 #pragma unroll
       for (int j = 0; j < kTopK; ++j) {
-        if (slots[j] < 0) break;
-        const size_t row = static_cast<size_t>(slots[j]);
-        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(y + row * H) + v);
-        const float f = __ldg(y_scale + row * ntile + tile);
-        const __half2* h = reinterpret_cast<const __half2*>(&raw);
+        const __half2* h = reinterpret_cast<const __half2*>(&raw[j]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 q = __half22float2(h[i]);
-          acc[2 * i] = fmaf(w[j], q.x * f, acc[2 * i]);
-          acc[2 * i + 1] = fmaf(w[j], q.y * f, acc[2 * i + 1]);
+          acc[2 * i] = fmaf(f[j], q.x, acc[2 * i]);
+          acc[2 * i + 1] = fmaf(f[j], q.y, acc[2 * i + 1]);
         }
       }
       uint4 o;
