@@ -299,6 +299,8 @@ def main():
         return reference_arm(args)
     if args.profile:
         return profile_once(args)
+    if args.workload in ("ep", "ep_hot"):
+        return ep_arm(args)
 
     world, rank, local = dist_setup(args.gpus)
     device = torch.device("cuda", local if world > 1 else 0)
@@ -416,6 +418,94 @@ def main():
         dist.destroy_process_group()
     if result is not None:
         print(json.dumps(result), flush=True)
+
+
+def ep_arm(args):
+    """global T=16384 tokens sharded evenly over N ranks, 256 experts sharded
+    contiguously (256/N per rank), NCCL dispatch/combine (flashinfer_b200.ep); strong scaling."""
+    from flashinfer_b200.ep import ExpertParallelMoE
+    world, rank, local = dist_setup(args.gpus)
+    device = torch.device("cuda", local if world > 1 else 0)
+    hot = 1.5 if args.workload == "ep_hot" else 0.0
+    seed = 11 if hot else 10
+    T_global = 16384
+    per = T_global // world
+    act = wl.make_activations(T_global, seed, hot_group=0 if hot else None, hot=hot)
+    rows = slice(rank * per, (rank + 1) * per)
+    host_in = [act.routing_logits[rows].contiguous(), act.routing_bias,
+               act.hidden_states[rows].contiguous(),
+               act.hidden_states_scale[:, rows].contiguous()]
+    epr = 256 // world
+    ws = [wl.expert_weights(e, device=str(device)) for e in range(rank * epr, (rank + 1) * epr)]
+    weights = [torch.stack([w[i] for w in ws]) for i in range(4)]
+    del ws
+    inp = [t.to(device) for t in host_in]
+    ep = ExpertParallelMoE()
+    out = torch.empty((per, wl.HIDDEN), dtype=torch.bfloat16, device=device)
+    for _ in range(args.warmup):
+        ep.forward(*inp, *weights, wl.RSF_DEFAULT, out)
+    barrier(world)
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(device.index or 0) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            ep.forward(*inp, *weights, wl.RSF_DEFAULT, out)
+        end.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps, world)
+    sent, recv = ep.last_counts
+    # end to end: pinned host inputs in, bf16 rows out, every step
+    pinned = [t.pin_memory() for t in host_in]
+    host_out = torch.empty((per, wl.HIDDEN), dtype=torch.bfloat16).pin_memory()
+    dev_in = [torch.empty_like(t, device=device) for t in pinned]
+    h2d = sum(t.numel() * t.element_size() for t in pinned)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def e2e_step():
+        for d, h in zip(dev_in, pinned):
+            d.copy_(h, non_blocking=True)
+        ep.forward(*dev_in, *weights, wl.RSF_DEFAULT, out)
+        host_out.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier(world)
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e2.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps, world)
+    if rank == 0:
+        from flashinfer_b200.ep import record_bytes
+        print(json.dumps({
+            "metric": METRIC, "value": round(T_global / (ms * 1e-3), 2), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "us_per_call": round(ms * 1e3, 1),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "e4m3",
+            "data": "synthetic (seeded activations; weights drawn on the GPU, same distributions)",
+            "config": {"workload": f"configs[4] expert parallel, global T={T_global}, "
+                                   f"{'hot group 0 (+1.5)' if hot else 'uniform'} logits, seed {seed}",
+                       "experts_per_gpu": epr, "tokens_per_gpu": per,
+                       "parallelism": f"ep{world} (NCCL all-to-all dispatch + combine)",
+                       "dispatch_records_rank0": sum(sent),
+                       "dispatch_bytes_rank0": sum(sent) * record_bytes(wl.HIDDEN),
+                       "combine_bytes_rank0": sum(sent) * wl.HIDDEN * 4,
+                       "received_tokens_rank0": sum(recv)},
+            "e2e": {"value": round(T_global / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                    "ms_per_step": round(e2e_ms, 4)},
+            "clocks": clocks.summary(),
+        }), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def profile_once(args):

@@ -28,6 +28,8 @@ ERRORS = {
 NOALLOC_MAX_TOKENS = 4096
 DTYPE_F32 = 0
 DTYPE_BF16 = 1
+OUT_BF16 = 0
+OUT_F32 = 1
 STOP_NONE, STOP_ROUTE, STOP_GATHER, STOP_GEMM1, STOP_GEMM2 = 0, 1, 2, 3, 4
 STATUS_TIMEOUT_GEMM1 = 0x1
 STATUS_TIMEOUT_GEMM2 = 0x2
@@ -65,6 +67,7 @@ class FmoeArgs(Structure):
         ("stop_after", c_int32),
         ("phase_events", c_void_p),
         ("num_phase_events", c_int32),
+        ("output_dtype", c_int32),
     ]
 
 

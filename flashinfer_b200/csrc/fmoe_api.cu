@@ -95,7 +95,8 @@ int validate(const FmoeArgs* a) {
       a->local_expert_offset + a->num_local_experts > a->num_experts)
     return FMOE_ERR_OFFSET;
   if ((a->logits_dtype != FMOE_DTYPE_F32 && a->logits_dtype != FMOE_DTYPE_BF16) ||
-      (a->bias_dtype != FMOE_DTYPE_F32 && a->bias_dtype != FMOE_DTYPE_BF16))
+      (a->bias_dtype != FMOE_DTYPE_F32 && a->bias_dtype != FMOE_DTYPE_BF16) ||
+      (a->output_dtype != FMOE_OUT_BF16 && a->output_dtype != FMOE_OUT_F32))
     return FMOE_ERR_DTYPE;
   if (a->num_tokens == 0) return FMOE_OK;
   const void* ptrs[] = {a->routing_logits, a->routing_bias,        a->hidden_states,
@@ -217,7 +218,8 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   p.hidden_scale = a->hidden_states_scale;
   p.w1_scale = a->gemm1_weights_scale;
   p.w2_scale = a->gemm2_weights_scale;
-  p.output = static_cast<__nv_bfloat16*>(a->output);
+  p.output = a->output;
+  p.out_f32 = a->output_dtype == FMOE_OUT_F32;
   p.T = T;
   p.H = H;
   p.I = I;

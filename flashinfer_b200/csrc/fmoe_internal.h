@@ -110,7 +110,8 @@ struct RunParams {
   const float* hidden_scale;   // [H/128, T]
   const float* w1_scale;       // [E, 2I/128, H/128]
   const float* w2_scale;       // [E, H/128, I/128]
-  __nv_bfloat16* output;       // [T, H]
+  void* output;                // [T, H] bf16, or fp32 when out_f32
+  int out_f32;
   int T, H, I, E, local_start;
   float rsf;
   // workspace

@@ -562,11 +562,25 @@ cudaError_t launch_route_permute(const void* logits, int logits_dtype, const voi
 // Y rows are fp16 with a power-of-two scale per 256 columns (exact to apply). Tokens without
 // local picks get zeros (kernel.py:692-695 zero-fills when nothing is local).
 // ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void store8(__nv_bfloat16* out, size_t v, const float (&acc)[8]) {
+  uint4 o;
+  __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) oh[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+  reinterpret_cast<uint4*>(out)[v] = o;
+}
+__device__ __forceinline__ void store8(float* out, size_t v, const float (&acc)[8]) {
+  float4* o = reinterpret_cast<float4*>(out) + 2 * v;
+  o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+
+template <typename TOut>
 __global__ void __launch_bounds__(128) k_combine(const int32_t* __restrict__ token_slot,
                                                  const float* __restrict__ token_weight,
                                                  const __half* __restrict__ y,
                                                  const float* __restrict__ y_scale, int T,
-                                                 int H, __nv_bfloat16* __restrict__ out) {
+                                                 int H, TOut* __restrict__ out) {
   const int nvec = H / 8;
   const int ntile = H / kTileN;
   for (int t = blockIdx.x; t < T; t += gridDim.x) {
@@ -606,11 +620,7 @@ __global__ void __launch_bounds__(128) k_combine(const int32_t* __restrict__ tok
           acc[2 * i + 1] = fmaf(f[j], q.y, acc[2 * i + 1]);
         }
       }
-      uint4 o;
-      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) oh[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-      reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H)[v] = o;
+      store8(out + static_cast<size_t>(t) * H, v, acc);
     }
   }
 }
@@ -620,11 +630,19 @@ cudaError_t launch_combine(const RunParams& p, cudaStream_t s) {
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
   int blocks = p.T < p.num_sms * 16 ? p.T : p.num_sms * 16;
-  k_combine<<<blocks, 128, 0, s>>>(reinterpret_cast<const int32_t*>(ws + L.token_slot),
-                                   reinterpret_cast<const float*>(ws + L.token_weight),
-                                   reinterpret_cast<const __half*>(ws + L.y_rows),
-                                   reinterpret_cast<const float*>(ws + L.y_scale), p.T, p.H,
-                                   p.output);
+  if (p.out_f32)
+    k_combine<float><<<blocks, 128, 0, s>>>(reinterpret_cast<const int32_t*>(ws + L.token_slot),
+                                            reinterpret_cast<const float*>(ws + L.token_weight),
+                                            reinterpret_cast<const __half*>(ws + L.y_rows),
+                                            reinterpret_cast<const float*>(ws + L.y_scale), p.T,
+                                            p.H, static_cast<float*>(p.output));
+  else
+    k_combine<__nv_bfloat16><<<blocks, 128, 0, s>>>(
+        reinterpret_cast<const int32_t*>(ws + L.token_slot),
+        reinterpret_cast<const float*>(ws + L.token_weight),
+        reinterpret_cast<const __half*>(ws + L.y_rows),
+        reinterpret_cast<const float*>(ws + L.y_scale), p.T, p.H,
+        static_cast<__nv_bfloat16*>(p.output));
   return cudaGetLastError();
 }
 

@@ -88,7 +88,9 @@ def _launch(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
             raise ValueError(f"{name} is on {t.device}, hidden_states on {device}")
     if output is None:
         output = torch.empty((T, hidden), dtype=torch.bfloat16, device=device)
-    _expect(output, "output", (T, hidden), torch.bfloat16)
+    _expect(output, "output", (T, hidden), None)
+    if output.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"output must be bfloat16 (or float32 for partial sums), got {output.dtype}")
 
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device)
@@ -122,6 +124,7 @@ def _launch(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
         a.workspace = ws.data_ptr()
         a.workspace_bytes = ws.numel()
         a.stop_after = int(stop_after)
+        a.output_dtype = _lib.OUT_F32 if output.dtype == torch.float32 else _lib.OUT_BF16
         rc = _lib.load().fmoe_run(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream))
     _lib.check(rc, "fmoe_run")
     return output, ws, lay

@@ -71,13 +71,18 @@ def quantize_activations(x_bf16: torch.Tensor):
     return q, scale.t().contiguous()
 
 
-def expert_weights(global_expert: int, hidden: int = HIDDEN, inter: int = INTER):
-    """Quantised (W1, S1, W2, S2) for one global expert, seeded 1000+id."""
-    g = torch.Generator().manual_seed(1000 + int(global_expert))
-    w1 = torch.randn(2 * inter, hidden, generator=g) * 0.02
+def expert_weights(global_expert: int, hidden: int = HIDDEN, inter: int = INTER,
+                   device: str = "cpu"):
+    """Quantised (W1, S1, W2, S2) for one global expert, seeded 1000+id.
+
+    With a CUDA ``device`` the draws come from that device's generator: same distributions,
+    different values than the CPU draws (used where only timing matters, never for parity).
+    """
+    g = torch.Generator(device=device).manual_seed(1000 + int(global_expert))
+    w1 = torch.randn(2 * inter, hidden, generator=g, device=device) * 0.02
     q1, s1 = _quantize_blocks_2d(w1)
     del w1
-    w2 = torch.randn(hidden, inter, generator=g) * 0.02
+    w2 = torch.randn(hidden, inter, generator=g, device=device) * 0.02
     q2, s2 = _quantize_blocks_2d(w2)
     return q1, s1, q2, s2
 
@@ -112,7 +117,7 @@ class Activations:
 
 def make_activations(T: int, seed: int, skew_experts: Optional[range] = None,
                      skew: float = 0.0, hot_group: Optional[int] = None,
-                     hot: float = 0.0) -> Activations:
+                     hot: float = 0.0, hidden: int = HIDDEN) -> Activations:
     """Seeded routing logits, bias and quantised hidden states (CPU)."""
     g = torch.Generator().manual_seed(int(seed))
     logits = torch.randn(T, E_GLOBAL, generator=g)
@@ -122,7 +127,7 @@ def make_activations(T: int, seed: int, skew_experts: Optional[range] = None,
         gs = E_GLOBAL // N_GROUP
         logits[:, hot_group * gs:(hot_group + 1) * gs] += hot
     bias = (torch.randn(E_GLOBAL, generator=g) * 0.1).to(torch.bfloat16)
-    hs = torch.randn(T, HIDDEN, generator=g).to(torch.bfloat16)
+    hs = torch.randn(T, hidden, generator=g).to(torch.bfloat16)
     q, s = quantize_activations(hs)
     return Activations(logits.contiguous(), bias.contiguous(), q.contiguous(), s)
 

@@ -49,6 +49,10 @@ extern "C" {
 #define FMOE_STATUS_TIMEOUT_GEMM1  0x1
 #define FMOE_STATUS_TIMEOUT_GEMM2  0x2
 
+/* output dtypes */
+#define FMOE_OUT_BF16    0
+#define FMOE_OUT_F32     1
+
 /* dtype tags for the routing inputs */
 #define FMOE_DTYPE_F32   0
 #define FMOE_DTYPE_BF16  1
@@ -100,6 +104,10 @@ typedef struct FmoeArgs {
    * [4] GEMM2 done, [5] combined. Extra entries are ignored; NULL entries are skipped. */
   void* const* phase_events;
   int32_t num_phase_events;
+  /* FMOE_OUT_BF16 (the reference's output, kernel.py:822) or FMOE_OUT_F32: the same sum left
+   * in fp32, for callers that add several partial outputs (expert parallelism) before the
+   * single final rounding to bf16. */
+  int32_t output_dtype;
 } FmoeArgs;
 
 /* Offsets (bytes from the workspace base) of the regions tests and tools read back. */
