@@ -11,7 +11,9 @@ import ctypes
 import os
 from ctypes import POINTER, Structure, byref, c_char_p, c_float, c_int32, c_int64, c_size_t, c_void_p
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libfmoe.so")
+# FLASHINFER_B200_LIB points at another build of the same library (A/B timing of two builds).
+LIB_PATH = os.environ.get("FLASHINFER_B200_LIB") or os.path.join(
+    os.path.dirname(os.path.abspath(__file__)), "_lib", "libfmoe.so")
 
 FMOE_OK = 0
 ERRORS = {

@@ -35,6 +35,20 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+// 2-D fp32 tensor map over a row-major [rows, cols] matrix, box = box_cols x 1 (unswizzled).
+bool make_tmap_f32_rows(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows,
+                        uint32_t box_cols) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 4};
+  const cuuint32_t box[2] = {box_cols, 1};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 2-D uint8 tensor map over a row-major [rows, cols] matrix with a 128-byte-swizzled box.
 bool make_tmap_u8(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows,
                   uint64_t row_stride, uint32_t box_cols, uint32_t box_rows) {
@@ -79,7 +93,7 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 int check_sizes(int T, int E, int H, int I) {
   if (T < 0 || E < 1 || E > kMaxLocalExperts) return FMOE_ERR_SHAPE;
   if (H <= 0 || I <= 0 || H % kTileN != 0 || I % kBlock != 0) return FMOE_ERR_SHAPE;
-  if (H / kBlock > 64 || I / kBlock > 64) return FMOE_ERR_SHAPE;  // staged scale rows
+  if (H / kBlock > 64 || I / kBlock > 64) return FMOE_ERR_SHAPE;  // GEMM weight-scale tables
   return FMOE_OK;
 }
 
@@ -241,17 +255,21 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   if (launch_scatter_gather(p, s) != cudaSuccess || !mark(2)) return FMOE_ERR_CUDA;
   if (a->stop_after == FMOE_STOP_ROUTE || a->stop_after == FMOE_STOP_GATHER) return FMOE_OK;
 
-  CUtensorMap tm_a, tm_w1, tm_hi, tm_lo, tm_w2;
+  CUtensorMap tm_a, tm_w1, tm_hi, tm_lo, tm_w2, tm_sa1, tm_sa2;
   if (!make_tmap_u8(&tm_a, p.ws + L.a_perm, H, L.cap, H, 128, 128) ||
       !make_tmap_u8(&tm_w1, a->gemm1_weights, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128) ||
       !make_tmap_u8(&tm_hi, p.ws + L.h_hi, I, L.cap, I, 128, 128) ||
       !make_tmap_u8(&tm_lo, p.ws + L.h_lo, I, L.cap, I, 128, 128) ||
-      !make_tmap_u8(&tm_w2, a->gemm2_weights, I, static_cast<uint64_t>(E) * H, I, 128, 256))
+      !make_tmap_u8(&tm_w2, a->gemm2_weights, I, static_cast<uint64_t>(E) * H, I, 128, 256) ||
+      // per-K-block activation scales, [K blocks][cap] fp32: one 128-slot row per load
+      !make_tmap_f32_rows(&tm_sa1, p.ws + L.a_scale_t, L.cap, H / kBlock, 128) ||
+      !make_tmap_f32_rows(&tm_sa2, p.ws + L.h_scale_t, L.cap, I / kBlock, 128))
     return FMOE_ERR_CUDA;
 
-  if (launch_gemm1(p, tm_a, tm_w1, s) != cudaSuccess || !mark(3)) return FMOE_ERR_CUDA;
+  if (launch_gemm1(p, tm_a, tm_w1, tm_sa1, s) != cudaSuccess || !mark(3)) return FMOE_ERR_CUDA;
   if (a->stop_after == FMOE_STOP_GEMM1) return FMOE_OK;
-  if (launch_gemm2(p, tm_hi, tm_lo, tm_w2, s) != cudaSuccess || !mark(4)) return FMOE_ERR_CUDA;
+  if (launch_gemm2(p, tm_hi, tm_lo, tm_w2, tm_sa2, s) != cudaSuccess || !mark(4))
+    return FMOE_ERR_CUDA;
   if (a->stop_after == FMOE_STOP_GEMM2) return FMOE_OK;
   if (launch_combine(p, s) != cudaSuccess || !mark(5)) return FMOE_ERR_CUDA;
   return FMOE_OK;

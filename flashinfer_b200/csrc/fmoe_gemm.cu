@@ -6,14 +6,18 @@
 //   KIND 2  <- _persistent_gemm2_kernel kernel.py:193-293 (the reference runs this GEMM in
 //              TF32 on an fp32 intermediate; here A = hi + lo e4m3 terms, two MMAs per K block)
 //
-// Per CTA (persistent, one per SM, 320 threads):
-//   warp 0      TMA producer: A tile [128 slots x 128 K] (+ the lo term for KIND 2) and the
-//               weight tile [256 rows x 128 K] into an NS-stage shared-memory ring.
+// Per CTA (persistent, one per SM, 352 threads):
+//   warps 0,10  TMA producers, alternating K iterations: A tile [128 slots x 128 K] (+ the lo
+//               term for KIND 2) and the weight tile [256 rows x 128 K] into an NS-stage
+//               shared-memory ring. One issuing warp sustains about 42 B/cycle per SM of
+//               128-row boxes; two sustain about 79 B/cycle, above the 48 KB per 520-cycle
+//               K block that the MMA consumes.
 //   warp 1      MMA issuer: per 128-wide K block, tcgen05.mma kind::f8f6f4 M=128 N=256 K=32
 //               x4 (x8 for KIND 2) into one of two TMEM partial buffers (2 x 256 columns).
 //   warps 2-9   promotion + epilogue: read each K block's partial from TMEM, scale it by
 //               a_scale[slot, kb] * w_scale[n-block, kb] and accumulate in fp32 registers
-//               (the reference's "partial * sa * sb" promotion, kernel.py:167-171).
+//               with packed FMA (the reference's "partial * sa * sb" promotion,
+//               kernel.py:167-171).
 // Work unit = (tile, K split). Tiles are ordered expert -> n-tile -> m-tile so concurrently
 // running CTAs share weight tiles in L2. When there are fewer tiles than SMs, the K range is
 // split; every split writes its partial tile, and the last one to arrive (an atomic counter)
@@ -61,10 +65,17 @@ struct Cfg<2> {
   static constexpr int STAGE = 128 * 128 * A_TILES + 256 * 128;  // 64 KB
 };
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 352;
 constexpr int kEpiWarps = 8;
+constexpr int kProducer2Warp = 10;
 constexpr int kTmemCols = 512;
 constexpr int kATileBytes = 128 * 128;
+// Activation scales of K iteration it land (by TMA, counted on full[s]) in ring entry it % 8.
+// The producer runs at most NS stages ahead of the MMA warp, which runs at most two K blocks
+// ahead of the epilogue, so an entry is never refilled before the epilogue has read it.
+constexpr int kSaRing = 8;
+constexpr int kSaBytes = 128 * 4;
+constexpr int kMaxKb = 64;  // K blocks per GEMM (H/128 and I/128); checked on the host
 
 struct GemmTail {
   uint64_t full[4];
@@ -76,14 +87,18 @@ struct GemmTail {
   int last_flag;
   int abort_flag;
   int pad_;
+  int last_issue[2][4];  // per producer, per stage: last round issued (-1 = none)
   float amax_x[2][128];
+  float w_sc[2][2][kMaxKb];  // [unit parity][tile half][K block] weight scales of a unit
   int ebase[kMaxLocalExperts + 1];
   int ecnt[kMaxLocalExperts];
 };
 
 template <int KIND>
 constexpr size_t gemm_smem_bytes() {
-  return static_cast<size_t>(Cfg<KIND>::NS) * Cfg<KIND>::STAGE + sizeof(GemmTail) + 1024;
+  static_assert(Cfg<KIND>::NS + 3 <= kSaRing, "activation-scale ring too short");
+  return static_cast<size_t>(Cfg<KIND>::NS) * Cfg<KIND>::STAGE + kSaRing * kSaBytes +
+         sizeof(GemmTail) + 1024;
 }
 
 struct Unit {
@@ -137,12 +152,92 @@ __device__ __forceinline__ void raise_abort(GemmTail* tail, int32_t* status, int
   atomicOr(status, code);
 }
 
+// Row maximum over the two column groups of epilogue warps that share a row (through shared
+// memory; every epilogue thread takes part).
+__device__ __forceinline__ float exchange_amax(GemmTail* tail, int g, int r, float amax) {
+  tail->amax_x[g][r] = amax;
+  named_bar_sync(1, kEpiWarps * 32);
+  return fmaxf(tail->amax_x[0][r], tail->amax_x[1][r]);
+}
+
+// Every lane polls the barrier; the warp agrees on the outcome.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int /*lane*/) {
+  const bool got = wait_or_abort(bar, parity, abort_flag);
+  return __all_sync(0xffffffffu, got);
+}
+
+// acc[0..16) += v[0..16) * f with packed fp32 FMA (same rounding as 16 fmaf).
+__device__ __forceinline__ void fma16(float* acc, const float* v, float f) {
+  const float2 ff = make_float2(f, f);
+#pragma unroll
+  for (int i = 0; i < 16; i += 2) {
+    const float2 r = __ffma2_rn(make_float2(v[i], v[i + 1]), ff, make_float2(acc[i], acc[i + 1]));
+    acc[i] = r.x;
+    acc[i + 1] = r.y;
+  }
+}
+
+// silu(up) * gate (moe.py:90-92) with the fast exponential and divide: relative error about
+// 1e-6, far below the e4m3 encoding that follows; for up < -87 the denominator is +inf and the
+// result is -0.
+__device__ __forceinline__ float swiglu(float up, float gate) {
+  return __fdividef(up, 1.0f + __expf(-up)) * gate;
+}
+
+// Two-term e4m3 encoding of 16 values: x * inv = hi + lo with hi = e4m3(x * inv) and
+// lo = e4m3(x * inv - hi); one 16-byte store per term.
+__device__ __forceinline__ void encode_e4m3_2term16(const float* x, float inv, uint4* hi_dst,
+                                                    uint4* lo_dst) {
+  uint32_t hw[4], lw[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    uint32_t hbits = 0, lbits = 0;
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr) {
+      const float x0 = x[w * 4 + pr * 2] * inv;
+      const float x1 = x[w * 4 + pr * 2 + 1] * inv;
+      const uint16_t hp = pack_e4m3x2(x0, x1);
+      const float2 back = unpack_e4m3x2(hp);
+      const uint16_t lp = pack_e4m3x2(x0 - back.x, x1 - back.y);
+      hbits |= static_cast<uint32_t>(hp) << (16 * pr);
+      lbits |= static_cast<uint32_t>(lp) << (16 * pr);
+    }
+    hw[w] = hbits;
+    lw[w] = lbits;
+  }
+  *hi_dst = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  *lo_dst = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+}
+
+// 16 values times a power-of-two inv, rounded to fp16, stored as two 16-byte words.
+__device__ __forceinline__ void store_f16x16(const float* x, float inv, __half* dst) {
+  uint32_t wv[8];
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const __half2 pr = __floats2half2_rn(x[2 * w] * inv, x[2 * w + 1] * inv);
+    wv[w] = *reinterpret_cast<const uint32_t*>(&pr);
+  }
+  reinterpret_cast<uint4*>(dst)[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  reinterpret_cast<uint4*>(dst)[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+}
+
+// Exponent k of the smallest 2^k with amax / 2^k <= 16384 (ceil(log2(amax)) - 14): the fp16
+// range is never exceeded, the scaling is exact and the relative precision stays 2^-11.
+__device__ __forceinline__ int pow2_exponent_for_f16(float amax) {
+  int ex = 0;
+  const float m = frexpf(amax, &ex);  // amax = m * 2^ex, m in [0.5, 1)
+  return (m > 0.5f ? ex : ex - 1) - 14;
+}
+
 template <int KIND>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
-           const __grid_constant__ CUtensorMap tm_w, const GemmArgs args) {
+           const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_sa,
+           const GemmArgs args) {
   using C = Cfg<KIND>;
   constexpr int NS = C::NS;
+  static_assert(NS >= 2 && NS <= 4, "barrier arrays hold 4 stages; alternating producers need 2");
   constexpr int STAGE = C::STAGE;
   constexpr int kErr = KIND == 1 ? FMOE_STATUS_TIMEOUT_GEMM1 : FMOE_STATUS_TIMEOUT_GEMM2;
 
@@ -153,7 +248,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-  GemmTail* tail = reinterpret_cast<GemmTail*>(smem + NS * STAGE);
+  float* sa_ring = reinterpret_cast<float*>(smem + NS * STAGE);  // [kSaRing][128]
+  GemmTail* tail = reinterpret_cast<GemmTail*>(smem + NS * STAGE + kSaRing * kSaBytes);
   volatile int* abort_flag = &tail->abort_flag;
 
   const int warp = threadIdx.x >> 5;
@@ -181,6 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tm_a0);
     if (KIND == 2) tma_prefetch_desc(&tm_a1);
     tma_prefetch_desc(&tm_w);
+    tma_prefetch_desc(&tm_sa);
   }
   if (warp == 1) {
     tmem_alloc(&tail->tmem_base, kTmemCols);
@@ -191,8 +288,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tail->tmem_base;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == kProducer2Warp) {
+    // ------------------------------------------------------------------ TMA producers
+    const int pw = warp == 0 ? 0 : 1;  // issues the K iterations it with (it & 1) == pw
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_a = policy_evict_last();
@@ -204,16 +302,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
         const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
         for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
+          if ((it & 1) != pw) continue;
           const int s = it % NS;
           const int r = it / NS;
+          // This producer issued iteration it - 2 after the release of it - 2 - NS, and the MMA
+          // warp releases in order, so round r - 2 of this stage is already released: the empty
+          // barrier is at most one phase behind and the parity wait is unambiguous.
           if (r > 0 && !wait_or_abort(&tail->empty[s], (r & 1) ^ 1, abort_flag)) {
             raise_abort(tail, args.status, kErr);
             ok = false;
             break;
           }
           uint8_t* st = smem + s * STAGE;
-          mbar_arrive_expect_tx(&tail->full[s], STAGE);
+          mbar_arrive_expect_tx(&tail->full[s], STAGE + kSaBytes);
           const int kx = kb * kBlock;
+          tma_load_2d(sa_ring + (it % kSaRing) * 128, &tm_sa, &tail->full[s], u.row0, kb, pol_a);
           if (KIND == 1) {
             const int wrow = u.e * 2 * args.I + u.n * kBlock;
             tma_load_2d(st, &tm_a0, &tail->full[s], kx, u.row0, pol_a);
@@ -228,10 +331,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           last_round[s] = r;
         }
       }
-      // Never leave a bulk copy in flight into shared memory that is about to be released.
 #pragma unroll
-      for (int s = 0; s < NS; ++s)
-        if (last_round[s] >= 0) (void)mbar_wait(&tail->full[s], last_round[s] & 1);
+      for (int s = 0; s < NS; ++s) tail->last_issue[pw][s] = last_round[s];
+    }
+    named_bar_sync(2, 64);
+    // Never leave a bulk copy in flight into shared memory that is about to be released. Each
+    // stage's latest round (over both producers) was issued after every earlier round of that
+    // stage had landed, so one wait per stage on the latest round suffices.
+    if (pw == 0 && lane == 0) {
+#pragma unroll
+      for (int s = 0; s < NS; ++s) {
+        const int r = max(tail->last_issue[0][s], tail->last_issue[1][s]);
+        if (r >= 0) (void)mbar_wait(&tail->full[s], r & 1);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
@@ -248,7 +360,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int rb = kt >> 1;
           if (!wait_or_abort(&tail->full[s], r & 1, abort_flag) ||
               (rb > 0 && !wait_or_abort(&tail->tempty[b], (rb & 1) ^ 1, abort_flag))) {
-            raise_abort(tail, args.status, kErr);
             ok = false;
             break;
           }
@@ -269,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(&tail->tfull[b]);
         }
       }
+      if (!ok) raise_abort(tail, args.status, kErr);
       mma_commit(&tail->drain);
       (void)mbar_wait(&tail->drain, 0);
     }
@@ -283,54 +395,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     int kt = 0;
     bool ok = true;
     float acc[128];
-    for (int unit = blockIdx.x; unit < units; unit += gridDim.x) {
-      const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
-      // every epilogue thread has finished the previous unit's shared-memory exchanges
-      named_bar_sync(1, kEpiWarps * 32);
-      // weight-scale rows of this tile's two 128-row halves (gate/up, or two n-blocks)
-      const float* sb0_ptr;
-      const float* sb1_ptr;
+    // Weight scales of a unit's two 128-row halves (gate/up, or two n-blocks) for all its K
+    // blocks (2 * nkb <= 128 values, one per epilogue thread), kept in w_sc[par]; a unit's
+    // table is fetched during the previous unit's epilogue and published by the unit-start
+    // barrier.
+    auto fetch_w_scale = [&](const Unit& uu) -> float {
+      if (etid >= 2 * nkb) return 0.0f;
+      const int h = etid >= nkb ? 1 : 0;
+      const int kb = etid - h * nkb;
+      size_t row;
       if (KIND == 1) {
         const int nb1 = args.I / kBlock;
-        const size_t base = static_cast<size_t>(u.e) * 2 * nb1;
-        sb0_ptr = args.w_scale + (base + u.n) * nkb;
-        sb1_ptr = args.w_scale + (base + nb1 + u.n) * nkb;
+        row = static_cast<size_t>(uu.e) * 2 * nb1 + h * nb1 + uu.n;
       } else {
-        const size_t base = static_cast<size_t>(u.e) * (args.H / kBlock);
-        sb0_ptr = args.w_scale + (base + 2 * u.n) * nkb;
-        sb1_ptr = args.w_scale + (base + 2 * u.n + 1) * nkb;
+        row = static_cast<size_t>(uu.e) * (args.H / kBlock) + 2 * uu.n + h;
       }
+      return __ldg(args.w_scale + row * nkb + kb);
+    };
+    auto store_w_scale = [&](int to_par, float v) {
+      if (etid < 2 * nkb) tail->w_sc[to_par][etid >= nkb ? 1 : 0][etid % nkb] = v;
+    };
+    int par = 0;
+    store_w_scale(0, fetch_w_scale(decode_unit(blockIdx.x, S, NT, nkb, tail->ebase, tail->ecnt, E)));
+    for (int unit = blockIdx.x; unit < units; unit += gridDim.x, par ^= 1) {
+      const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
+      // every epilogue thread has finished the previous unit and written this unit's w_sc
+      named_bar_sync(1, kEpiWarps * 32);
       // Warps whose 32 rows are all padding skip the TMEM reads (their rows are discarded);
-      // they still wait for each buffer before releasing it, which keeps the phases aligned.
+      // they still wait for each half before releasing it, which keeps the phases aligned.
       const bool warp_rows = q * 32 < u.nrows;
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
-      const float* sa_ptr = args.a_scale_t + u.row0 + r;
-      float sa_next = 0.0f, sb0_next = 0.0f, sb1_next = 0.0f;
-      if (u.kb0 < u.kb1) {
-        sa_next = __ldg(sa_ptr + static_cast<int64_t>(u.kb0) * cap);
-        sb0_next = __ldg(sb0_ptr + u.kb0);
-        sb1_next = __ldg(sb1_ptr + u.kb0);
-      }
+      const bool has_next = unit + static_cast<int>(gridDim.x) < units;
+      float w_next = 0.0f;  // the next unit's weight scale, fetched during the last K block
       for (int kb = u.kb0; kb < u.kb1; ++kb, ++kt) {
-        const float sa = sa_next, sb0 = sb0_next, sb1 = sb1_next;
-        if (kb + 1 < u.kb1) {
-          sa_next = __ldg(sa_ptr + static_cast<int64_t>(kb + 1) * cap);
-          sb0_next = __ldg(sb0_ptr + kb + 1);
-          sb1_next = __ldg(sb1_ptr + kb + 1);
-        }
+        if (has_next && kb == u.kb1 - 1)
+          w_next = fetch_w_scale(decode_unit(unit + gridDim.x, S, NT, nkb, tail->ebase,
+                                             tail->ecnt, E));
+        if (!ok) continue;
         const int b = kt & 1;
         const int rb = kt >> 1;
-        bool got = ok && wait_or_abort(&tail->tfull[b], rb & 1, abort_flag);
-        got = __all_sync(0xffffffffu, got);
-        if (!got && ok) {
+        if (!warp_wait(&tail->tfull[b], rb & 1, abort_flag, lane)) {
           if (lane == 0) raise_abort(tail, args.status, kErr);
           ok = false;
+          continue;
         }
-        if (got && warp_rows) {
+        if (warp_rows) {
           tc_fence_after();
-          const float f0 = sa * sb0;
-          const float f1 = sa * sb1;
+          // the activation scale reached shared memory before the MMA that this wait follows
+          const float sa = sa_ring[(kt % kSaRing) * 128 + r];
+          const float f0 = sa * tail->w_sc[par][0][kb];
+          const float f1 = sa * tail->w_sc[par][1][kb];
           const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kTileN;
           // 8 chunks of 16 columns: gate (or n-block 0) cols g*64 + [0,64), then up (n-block 1)
           // cols 128 + g*64 + [0,64). Chunk c+1 is in flight while chunk c is accumulated.
@@ -344,25 +459,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float f = c < 4 ? f0 : f1;
             if ((c & 1) == 0) {
               if (cn < 8) tmem_ld_32x32b_x16(taddr + coln, vb);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(va[i], f, acc[c * 16 + i]);
+              fma16(acc + c * 16, va, f);
               if (cn < 8) tmem_ld_wait16(vb);
             } else {
               if (cn < 8) tmem_ld_32x32b_x16(taddr + coln, va);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(vb[i], f, acc[c * 16 + i]);
+              fma16(acc + c * 16, vb, f);
               if (cn < 8) tmem_ld_wait16(va);
             }
           }
           tc_fence_before();
         }
         __syncwarp();
-        if (got && lane == 0) mbar_arrive(&tail->tempty[b]);
+        if (lane == 0) mbar_arrive(&tail->tempty[b]);
       }
+      // w_sc[par ^ 1] was last read in the previous unit, which every epilogue thread has left
+      if (has_next) store_w_scale(par ^ 1, w_next);
 
       const bool valid = r < u.nrows;
+      const size_t row = static_cast<size_t>(u.row0) + r;
       if (S > 1) {
-        // split-K: publish this split's partial tile, the last arriver reduces in split order
+        // split-K: publish this split's partial tile; the last arriver sums the splits in split
+        // order and runs the epilogue straight from the partials, 16 columns at a time (the
+        // accumulators are dead on this path, which keeps it from adding register pressure
+        // to the main one)
         const int tile = unit / S;
         const int slot_rows = args.partial_rows;
         if (valid) {
@@ -385,26 +504,72 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar_sync(1, kEpiWarps * 32);
         if (!tail->last_flag) continue;
         __threadfence();
-        if (valid) {
+        const float* p0 = args.partials + (static_cast<size_t>(tile * S) * slot_rows + r) * kTileN;
+        const size_t split_stride = static_cast<size_t>(slot_rows) * kTileN;
+        // columns [col, col + 16) of this thread's row, summed over the splits in split order
+        auto split_sum16 = [&](int col, float* v) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+          for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+          if (!valid) return;
           for (int sp = 0; sp < S; ++sp) {
-            const float* p =
-                args.partials + (static_cast<size_t>(tile * S + sp) * slot_rows + r) * kTileN;
+            const float4* src = reinterpret_cast<const float4*>(p0 + sp * split_stride + col);
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const float4* src = reinterpret_cast<const float4*>(p + h * 128 + g * 64);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) {
-                const float4 v = __ldcg(src + i);
-                acc[h * 64 + 4 * i] += v.x;
-                acc[h * 64 + 4 * i + 1] += v.y;
-                acc[h * 64 + 4 * i + 2] += v.z;
-                acc[h * 64 + 4 * i + 3] += v.w;
-              }
+            for (int i = 0; i < 4; ++i) {
+              const float4 x = __ldcg(src + i);
+              v[4 * i] += x.x;
+              v[4 * i + 1] += x.y;
+              v[4 * i + 2] += x.z;
+              v[4 * i + 3] += x.w;
             }
           }
+        };
+        if (KIND == 1) {
+          auto h16 = [&](int cc, float* h) {
+            float gate[16];
+            split_sum16(g * 64 + cc * 16, gate);
+            split_sum16(128 + g * 64 + cc * 16, h);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) h[i] = valid ? swiglu(h[i], gate[i]) : 0.0f;
+          };
+          float amax = 0.0f;
+          for (int cc = 0; cc < 4; ++cc) {
+            float h[16];
+            h16(cc, h);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
+          }
+          amax = exchange_amax(tail, g, r, amax);
+          const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
+          uint4* hi_dst = reinterpret_cast<uint4*>(args.h_hi + row * args.I + u.n * kBlock + g * 64);
+          uint4* lo_dst = reinterpret_cast<uint4*>(args.h_lo + row * args.I + u.n * kBlock + g * 64);
+          for (int cc = 0; cc < 4; ++cc) {
+            float h[16];
+            h16(cc, h);
+            encode_e4m3_2term16(h, inv, hi_dst + cc, lo_dst + cc);
+          }
+          if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = amax / 448.0f;
+        } else {
+          float amax = 0.0f;
+          for (int cc = 0; cc < 8; ++cc) {
+            float v[16];
+            split_sum16((cc >> 2) * 128 + g * 64 + (cc & 3) * 16, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+          }
+          amax = exchange_amax(tail, g, r, amax);
+          const int k = pow2_exponent_for_f16(amax);
+          const float inv = ldexpf(1.0f, -k);
+          if (valid) {
+            for (int cc = 0; cc < 8; ++cc) {
+              float v[16];
+              split_sum16((cc >> 2) * 128 + g * 64 + (cc & 3) * 16, v);
+              store_f16x16(v, inv, args.y + row * args.H + u.n * kTileN + (cc >> 2) * 128 +
+                                       g * 64 + (cc & 3) * 16);
+            }
+            if (g == 0) args.y_scale[row * (args.H / kTileN) + u.n] = ldexpf(1.0f, k);
+          }
         }
+        continue;
       }
 
       if (KIND == 1) {
@@ -413,80 +578,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         float amax = 0.0f;
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const float gate = acc[c];
-          const float up = acc[64 + c];
-          const float h = valid ? (up / (1.0f + expf(-up))) * gate : 0.0f;
+          const float h = valid ? swiglu(acc[64 + c], acc[c]) : 0.0f;
           acc[c] = h;
           amax = fmaxf(amax, fabsf(h));
         }
-        tail->amax_x[g][r] = amax;
-        named_bar_sync(1, kEpiWarps * 32);
-        amax = fmaxf(tail->amax_x[0][r], tail->amax_x[1][r]);
+        amax = exchange_amax(tail, g, r, amax);
         const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
-        const float scale = amax / 448.0f;
-        const size_t row = static_cast<size_t>(u.row0) + r;
-        uint4* hi_dst =
-            reinterpret_cast<uint4*>(args.h_hi + row * args.I + u.n * kBlock + g * 64);
-        uint4* lo_dst =
-            reinterpret_cast<uint4*>(args.h_lo + row * args.I + u.n * kBlock + g * 64);
+        uint4* hi_dst = reinterpret_cast<uint4*>(args.h_hi + row * args.I + u.n * kBlock + g * 64);
+        uint4* lo_dst = reinterpret_cast<uint4*>(args.h_lo + row * args.I + u.n * kBlock + g * 64);
 #pragma unroll
-        for (int v16 = 0; v16 < 4; ++v16) {
-          uint32_t hw[4], lw[4];
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            uint32_t hbits = 0, lbits = 0;
-#pragma unroll
-            for (int pr = 0; pr < 2; ++pr) {
-              const int c = v16 * 16 + w * 4 + pr * 2;
-              const float x0 = acc[c] * inv;
-              const float x1 = acc[c + 1] * inv;
-              const uint16_t hp = pack_e4m3x2(x0, x1);
-              const float2 back = unpack_e4m3x2(hp);
-              const uint16_t lp = pack_e4m3x2(x0 - back.x, x1 - back.y);
-              hbits |= static_cast<uint32_t>(hp) << (16 * pr);
-              lbits |= static_cast<uint32_t>(lp) << (16 * pr);
-            }
-            hw[w] = hbits;
-            lw[w] = lbits;
-          }
-          hi_dst[v16] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-          lo_dst[v16] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
-        if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = scale;
+        for (int cc = 0; cc < 4; ++cc) encode_e4m3_2term16(acc + cc * 16, inv, hi_dst + cc, lo_dst + cc);
+        if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = amax / 448.0f;
       } else {
-        // fp16 rows with one power-of-two scale per slot per 256 columns: the smallest 2^k
-        // with amax / 2^k <= 16384, so the fp16 range is never exceeded and the scaling is
-        // exact; relative precision stays 2^-11.
         float amax = 0.0f;
         if (valid) {
 #pragma unroll
           for (int c = 0; c < 128; ++c) amax = fmaxf(amax, fabsf(acc[c]));
         }
-        tail->amax_x[g][r] = amax;
-        named_bar_sync(1, kEpiWarps * 32);
-        amax = fmaxf(tail->amax_x[0][r], tail->amax_x[1][r]);
-        int ex = 0;
-        const float m = frexpf(amax, &ex);          // amax = m * 2^ex, m in [0.5, 1)
-        const int k = (m > 0.5f ? ex : ex - 1) - 14;  // ceil(log2(amax)) - 14
+        amax = exchange_amax(tail, g, r, amax);
+        const int k = pow2_exponent_for_f16(amax);
         const float inv = ldexpf(1.0f, -k);
         if (valid) {
-          const size_t row = static_cast<size_t>(u.row0) + r;
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            uint4* dst = reinterpret_cast<uint4*>(args.y + row * args.H + u.n * kTileN + h * 128 +
-                                                  g * 64);
-#pragma unroll
-            for (int v8 = 0; v8 < 8; ++v8) {
-              uint32_t wv[4];
-#pragma unroll
-              for (int w = 0; w < 4; ++w) {
-                const __half2 pr = __floats2half2_rn(acc[h * 64 + v8 * 8 + 2 * w] * inv,
-                                                     acc[h * 64 + v8 * 8 + 2 * w + 1] * inv);
-                wv[w] = *reinterpret_cast<const uint32_t*>(&pr);
-              }
-              dst[v8] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-            }
-          }
+          for (int cc = 0; cc < 8; ++cc)
+            store_f16x16(acc + cc * 16, inv, args.y + row * args.H + u.n * kTileN +
+                                                 (cc >> 2) * 128 + g * 64 + (cc & 3) * 16);
           if (g == 0) args.y_scale[row * (args.H / kTileN) + u.n] = ldexpf(1.0f, k);
         }
       }
@@ -505,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 template <int KIND>
 static cudaError_t launch_gemm_kind(const RunParams& p, const CUtensorMap& a0,
                                     const CUtensorMap& a1, const CUtensorMap& w,
-                                    cudaStream_t s) {
+                                    const CUtensorMap& sa, cudaStream_t s) {
   const size_t smem = gemm_smem_bytes<KIND>();
   static int configured_device = -1;
   int dev = 0;
@@ -537,18 +653,18 @@ static cudaError_t launch_gemm_kind(const RunParams& p, const CUtensorMap& a0,
   a.I = p.I;
   a.cap = L.cap;
   a.partial_rows = static_cast<int>(L.partial_rows);
-  k_gemm<KIND><<<p.num_sms, kThreads, smem, s>>>(a0, a1, w, a);
+  k_gemm<KIND><<<p.num_sms, kThreads, smem, s>>>(a0, a1, w, sa, a);
   return cudaGetLastError();
 }
 
 cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUtensorMap& tm_w1,
-                         cudaStream_t s) {
-  return launch_gemm_kind<1>(p, tm_a, tm_a, tm_w1, s);
+                         const CUtensorMap& tm_sa, cudaStream_t s) {
+  return launch_gemm_kind<1>(p, tm_a, tm_a, tm_w1, tm_sa, s);
 }
 
 cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
-                         const CUtensorMap& tm_w2, cudaStream_t s) {
-  return launch_gemm_kind<2>(p, tm_hi, tm_lo, tm_w2, s);
+                         const CUtensorMap& tm_w2, const CUtensorMap& tm_sa, cudaStream_t s) {
+  return launch_gemm_kind<2>(p, tm_hi, tm_lo, tm_w2, tm_sa, s);
 }
 
 }  // namespace fmoe

@@ -128,9 +128,9 @@ cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s);
 cudaError_t launch_scan(const RunParams& p, cudaStream_t s);
 cudaError_t launch_scatter_gather(const RunParams& p, cudaStream_t s);
 cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUtensorMap& tm_w1,
-                         cudaStream_t s);
+                         const CUtensorMap& tm_sa, cudaStream_t s);
 cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
-                         const CUtensorMap& tm_w2, cudaStream_t s);
+                         const CUtensorMap& tm_w2, const CUtensorMap& tm_sa, cudaStream_t s);
 cudaError_t launch_combine(const RunParams& p, cudaStream_t s);
 
 // Routing + permutation with every buffer passed explicitly (used by the entry point whose
