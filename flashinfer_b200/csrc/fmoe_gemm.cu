@@ -240,6 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(NS >= 2 && NS <= 4, "barrier arrays hold 4 stages; alternating producers need 2");
   constexpr int STAGE = C::STAGE;
   constexpr int kErr = KIND == 1 ? FMOE_STATUS_TIMEOUT_GEMM1 : FMOE_STATUS_TIMEOUT_GEMM2;
+  pdl_begin();
 
   const int S = args.plan[KIND == 1 ? kPlanSplit1 : kPlanSplit2];
   const int units = args.plan[KIND == 1 ? kPlanUnits1 : kPlanUnits2];
@@ -442,15 +443,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (warp_rows) {
           tc_fence_after();
-          // the activation scale reached shared memory before the MMA that this wait follows
-          const float sa = sa_ring[(kt % kSaRing) * 128 + r];
-          const float f0 = sa * tail->w_sc[par][0][kb];
-          const float f1 = sa * tail->w_sc[par][1][kb];
           const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kTileN;
           // 8 chunks of 16 columns: gate (or n-block 0) cols g*64 + [0,64), then up (n-block 1)
           // cols 128 + g*64 + [0,64). Chunk c+1 is in flight while chunk c is accumulated.
           float va[16], vb[16];
           tmem_ld_32x32b_x16(taddr + g * 64, va);
+          // the activation scale reached shared memory before the MMA that this wait follows;
+          // the shared-memory reads overlap the first TMEM load
+          const float sa = sa_ring[(kt % kSaRing) * 128 + r];
+          const float f0 = sa * tail->w_sc[par][0][kb];
+          const float f1 = sa * tail->w_sc[par][1][kb];
           tmem_ld_wait16(va);
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
@@ -529,25 +531,31 @@ __global__ void __launch_bounds__(kThreads, 1)
             split_sum16(g * 64 + cc * 16, gate);
             split_sum16(128 + g * 64 + cc * 16, h);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) h[i] = valid ? swiglu(h[i], gate[i]) : 0.0f;
+            for (int i = 0; i < 16; ++i) h[i] = swiglu(h[i], gate[i]);
           };
           float amax = 0.0f;
-          for (int cc = 0; cc < 4; ++cc) {
-            float h[16];
-            h16(cc, h);
+          if (valid) {
+            for (int cc = 0; cc < 4; ++cc) {
+              float h[16];
+              h16(cc, h);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
+              for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
+            }
           }
           amax = exchange_amax(tail, g, r, amax);
-          const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
-          uint4* hi_dst = reinterpret_cast<uint4*>(args.h_hi + row * args.I + u.n * kBlock + g * 64);
-          uint4* lo_dst = reinterpret_cast<uint4*>(args.h_lo + row * args.I + u.n * kBlock + g * 64);
-          for (int cc = 0; cc < 4; ++cc) {
-            float h[16];
-            h16(cc, h);
-            encode_e4m3_2term16(h, inv, hi_dst + cc, lo_dst + cc);
+          if (valid) {
+            const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
+            uint4* hi_dst =
+                reinterpret_cast<uint4*>(args.h_hi + row * args.I + u.n * kBlock + g * 64);
+            uint4* lo_dst =
+                reinterpret_cast<uint4*>(args.h_lo + row * args.I + u.n * kBlock + g * 64);
+            for (int cc = 0; cc < 4; ++cc) {
+              float h[16];
+              h16(cc, h);
+              encode_e4m3_2term16(h, inv, hi_dst + cc, lo_dst + cc);
+            }
+            if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = amax / 448.0f;
           }
-          if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = amax / 448.0f;
         } else {
           float amax = 0.0f;
           for (int cc = 0; cc < 8; ++cc) {
@@ -574,21 +582,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       if (KIND == 1) {
         // SwiGLU (moe.py:90-92: silu(second half) * first half), then the two-term e4m3
-        // encoding with one scale per slot per 128 intermediate columns.
+        // encoding with one scale per slot per 128 intermediate columns. Padding slots are
+        // skipped: GEMM2 only writes the output rows of valid slots, so their intermediate
+        // rows and scales are never read into a result.
         float amax = 0.0f;
+        if (valid) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float h = valid ? swiglu(acc[64 + c], acc[c]) : 0.0f;
-          acc[c] = h;
-          amax = fmaxf(amax, fabsf(h));
+          for (int c = 0; c < 64; ++c) {
+            const float h = swiglu(acc[64 + c], acc[c]);
+            acc[c] = h;
+            amax = fmaxf(amax, fabsf(h));
+          }
         }
         amax = exchange_amax(tail, g, r, amax);
-        const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
-        uint4* hi_dst = reinterpret_cast<uint4*>(args.h_hi + row * args.I + u.n * kBlock + g * 64);
-        uint4* lo_dst = reinterpret_cast<uint4*>(args.h_lo + row * args.I + u.n * kBlock + g * 64);
+        if (valid) {
+          const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
+          uint4* hi_dst = reinterpret_cast<uint4*>(args.h_hi + row * args.I + u.n * kBlock + g * 64);
+          uint4* lo_dst = reinterpret_cast<uint4*>(args.h_lo + row * args.I + u.n * kBlock + g * 64);
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) encode_e4m3_2term16(acc + cc * 16, inv, hi_dst + cc, lo_dst + cc);
-        if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = amax / 448.0f;
+          for (int cc = 0; cc < 4; ++cc)
+            encode_e4m3_2term16(acc + cc * 16, inv, hi_dst + cc, lo_dst + cc);
+          if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = amax / 448.0f;
+        }
       } else {
         float amax = 0.0f;
         if (valid) {
@@ -653,7 +668,7 @@ static cudaError_t launch_gemm_kind(const RunParams& p, const CUtensorMap& a0,
   a.I = p.I;
   a.cap = L.cap;
   a.partial_rows = static_cast<int>(L.partial_rows);
-  k_gemm<KIND><<<p.num_sms, kThreads, smem, s>>>(a0, a1, w, sa, a);
+  (void)launch_pdl(k_gemm<KIND>, p.num_sms, kThreads, smem, s, a0, a1, w, sa, a);
   return cudaGetLastError();
 }
 

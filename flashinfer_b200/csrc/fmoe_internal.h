@@ -157,4 +157,31 @@ cudaError_t launch_route_permute(const void* logits, int logits_dtype, const voi
                                  int H, int I, int num_sms, const PermuteBuffers& b,
                                  cudaStream_t s);
 
+// ---------------------------------------------------------------- programmatic dependent launch
+// Every kernel of the path is launched with programmatic stream serialisation. A kernel first
+// lets the next kernel in the stream be scheduled (its CTAs are placed as resources free up and
+// park in griddepcontrol.wait), then waits for the previous grid to complete and its memory to
+// become visible before it reads anything. Results are the same as plain stream order; the
+// launch latency between the seven kernels of a call overlaps the previous kernel's tail.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 }  // namespace fmoe

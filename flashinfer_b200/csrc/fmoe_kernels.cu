@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(256) k_route(const TL* __restrict__ logits,
                                                const TB* __restrict__ bias, int T, float rsf,
                                                int32_t* __restrict__ ids_out,
                                                float* __restrict__ w_out) {
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int warp0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nwarps = gridDim.x * (blockDim.x >> 5);
@@ -182,6 +183,7 @@ __global__ void __launch_bounds__(256) k_route_hist(const TL* __restrict__ logit
                                                     float* __restrict__ w_out,
                                                     int32_t* __restrict__ block_hist) {
   __shared__ int hist[kMaxLocalExperts];
+  pdl_begin();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
@@ -216,19 +218,19 @@ cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias,
   if (blocks > 148 * 16) blocks = 148 * 16;
   const dim3 grid(blocks), block(warps_per_block * 32);
   if (logits_dtype == FMOE_DTYPE_F32 && bias_dtype == FMOE_DTYPE_BF16)
-    k_route<float, __nv_bfloat16><<<grid, block, 0, s>>>(
+    (void)launch_pdl(k_route<float, __nv_bfloat16>, grid, block, 0, s,
         static_cast<const float*>(logits), static_cast<const __nv_bfloat16*>(bias), T, rsf,
         topk_ids, topk_w);
   else if (logits_dtype == FMOE_DTYPE_F32 && bias_dtype == FMOE_DTYPE_F32)
-    k_route<float, float><<<grid, block, 0, s>>>(static_cast<const float*>(logits),
+    (void)launch_pdl(k_route<float, float>, grid, block, 0, s, static_cast<const float*>(logits),
                                                   static_cast<const float*>(bias), T, rsf,
                                                   topk_ids, topk_w);
   else if (logits_dtype == FMOE_DTYPE_BF16 && bias_dtype == FMOE_DTYPE_BF16)
-    k_route<__nv_bfloat16, __nv_bfloat16><<<grid, block, 0, s>>>(
+    (void)launch_pdl(k_route<__nv_bfloat16, __nv_bfloat16>, grid, block, 0, s,
         static_cast<const __nv_bfloat16*>(logits), static_cast<const __nv_bfloat16*>(bias), T,
         rsf, topk_ids, topk_w);
   else
-    k_route<__nv_bfloat16, float><<<grid, block, 0, s>>>(
+    (void)launch_pdl(k_route<__nv_bfloat16, float>, grid, block, 0, s,
         static_cast<const __nv_bfloat16*>(logits), static_cast<const float*>(bias), T, rsf,
         topk_ids, topk_w);
   return cudaGetLastError();
@@ -275,6 +277,7 @@ __global__ void __launch_bounds__(1024) k_scan(const int32_t* __restrict__ block
   __shared__ int sh[kMaxBlockCounts];
   __shared__ int cnt[kMaxLocalExperts];
   __shared__ int base[kMaxLocalExperts + 1];
+  pdl_begin();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
   const int n = nblocks * E;
   for (int i = threadIdx.x; i < n; i += blockDim.x) sh[i] = block_hist[i];
@@ -343,6 +346,7 @@ __global__ void __launch_bounds__(256) k_scatter(
     int32_t* __restrict__ slot_token, float* __restrict__ slot_weight,
     int32_t* __restrict__ token_slot, float* __restrict__ token_weight) {
   __shared__ ScatterSmem sm;
+  pdl_begin();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.x;
   const int t_begin = b * tpb;
@@ -441,6 +445,7 @@ __global__ void __launch_bounds__(256) k_gather_tokens(const int32_t* __restrict
                                                        uint8_t* __restrict__ a_perm,
                                                        float* __restrict__ a_scale_t) {
   constexpr int kMaxVec = 16;  // H <= 8192 (at most 64 scale blocks; 16 B per lane per step)
+  pdl_begin();
   const int lane = threadIdx.x & 31;
   const int warp0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nwarps = gridDim.x * (blockDim.x >> 5);
@@ -485,7 +490,7 @@ cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s) {
   return dispatch_dtypes(p.logits_dtype, p.bias_dtype, [&](auto tl, auto tb) {
     using TL = decltype(tl);
     using TB = decltype(tb);
-    k_route_hist<TL, TB><<<L.nblocks, 256, 0, s>>>(
+    (void)launch_pdl(k_route_hist<TL, TB>, L.nblocks, 256, 0, s,
         static_cast<const TL*>(p.logits), static_cast<const TB*>(p.bias), p.T, L.tpb, p.rsf,
         p.local_start, p.E, reinterpret_cast<int32_t*>(ws + L.topk_ids),
         reinterpret_cast<float*>(ws + L.topk_w), reinterpret_cast<int32_t*>(ws + L.block_hist));
@@ -496,7 +501,7 @@ cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s) {
 cudaError_t launch_scan(const RunParams& p, cudaStream_t s) {
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
-  k_scan<<<1, 1024, 0, s>>>(reinterpret_cast<const int32_t*>(ws + L.block_hist), L.nblocks, p.E,
+  (void)launch_pdl(k_scan, 1, 1024, 0, s, reinterpret_cast<const int32_t*>(ws + L.block_hist), L.nblocks, p.E,
                             p.H, p.I, p.num_sms, reinterpret_cast<int32_t*>(ws + L.block_off),
                             reinterpret_cast<int32_t*>(ws + L.plan),
                             reinterpret_cast<int32_t*>(ws + L.expert_count),
@@ -510,7 +515,7 @@ cudaError_t launch_scatter_gather(const RunParams& p, cudaStream_t s) {
   if (p.T <= 0) return cudaSuccess;
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
-  k_scatter<<<L.nblocks, 256, 0, s>>>(
+  (void)launch_pdl(k_scatter, L.nblocks, 256, 0, s,
       reinterpret_cast<const int32_t*>(ws + L.topk_ids),
       reinterpret_cast<const float*>(ws + L.topk_w), p.T, L.tpb, p.local_start, p.E,
       reinterpret_cast<const int32_t*>(ws + L.block_off),
@@ -523,7 +528,7 @@ cudaError_t launch_scatter_gather(const RunParams& p, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   int blocks = (p.T + 7) / 8;
   if (blocks > p.num_sms * 8) blocks = p.num_sms * 8;
-  k_gather_tokens<<<blocks, 256, 0, s>>>(reinterpret_cast<const int32_t*>(ws + L.token_slot),
+  (void)launch_pdl(k_gather_tokens, blocks, 256, 0, s, reinterpret_cast<const int32_t*>(ws + L.token_slot),
                                          p.hidden, p.hidden_scale, p.T, p.H, L.cap,
                                          ws + L.a_perm, reinterpret_cast<float*>(ws + L.a_scale_t));
   return cudaGetLastError();
@@ -539,26 +544,27 @@ cudaError_t launch_route_permute(const void* logits, int logits_dtype, const voi
   cudaError_t e = dispatch_dtypes(logits_dtype, bias_dtype, [&](auto tl, auto tb) {
     using TL = decltype(tl);
     using TB = decltype(tb);
-    k_route_hist<TL, TB><<<nblocks, 256, 0, s>>>(static_cast<const TL*>(logits),
+    (void)launch_pdl(k_route_hist<TL, TB>, nblocks, 256, 0, s, static_cast<const TL*>(logits),
                                                   static_cast<const TB*>(bias), T, tpb, rsf,
                                                   local_start, E, bf.topk_ids, bf.topk_w,
                                                   bf.block_hist);
     return cudaGetLastError();
   });
   if (e != cudaSuccess) return e;
-  k_scan<<<1, 1024, 0, s>>>(bf.block_hist, nblocks, E, H, I, num_sms, bf.block_off, bf.plan,
+  (void)launch_pdl(k_scan, 1, 1024, 0, s, bf.block_hist, nblocks, E, H, I, num_sms, bf.block_off, bf.plan,
                             bf.expert_count, bf.expert_base, bf.counters, bf.status);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  k_scatter<<<nblocks, 256, 0, s>>>(bf.topk_ids, bf.topk_w, T, tpb, local_start, E,
+  (void)launch_pdl(k_scatter, nblocks, 256, 0, s, bf.topk_ids, bf.topk_w, T, tpb, local_start, E,
                                     bf.block_off, bf.expert_count, bf.expert_base, bf.slot_token,
                                     bf.slot_weight, bf.token_slot, bf.token_weight);
   return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------------------------------
-// Combine: one CTA per token sums w * Y[slot] over the token's local picks in ascending
-// expert order (the definition's loop order, moe.py:79-98), in registers, then writes bf16.
+// Combine: one CTA per (token, 8 * blockDim columns) sums w * Y[slot] over the token's local
+// picks in ascending expert order (the definition's loop order, moe.py:79-98), in registers,
+// then writes bf16; small T still spreads over every SM.
 // Y rows are fp16 with a power-of-two scale per 256 columns (exact to apply). Tokens without
 // local picks get zeros (kernel.py:692-695 zero-fills when nothing is local).
 // ------------------------------------------------------------------------------------------
@@ -575,53 +581,64 @@ __device__ __forceinline__ void store8(float* out, size_t v, const float (&acc)[
   o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
+// Each thread owns kCombineVec consecutive 16-byte vectors (32 columns, inside one 256-column
+// scale tile) of one token's row: per local pick it issues all of that pick's loads at once, so
+// a thread keeps 64 bytes in flight; the picks are added in ascending expert order.
+constexpr int kCombineVec = 4;
+constexpr int kCombineThreads = 128;
+
 template <typename TOut>
-__global__ void __launch_bounds__(128) k_combine(const int32_t* __restrict__ token_slot,
-                                                 const float* __restrict__ token_weight,
-                                                 const __half* __restrict__ y,
-                                                 const float* __restrict__ y_scale, int T,
-                                                 int H, TOut* __restrict__ out) {
+__global__ void __launch_bounds__(kCombineThreads) k_combine(const int32_t* __restrict__ token_slot,
+                                                             const float* __restrict__ token_weight,
+                                                             const __half* __restrict__ y,
+                                                             const float* __restrict__ y_scale,
+                                                             int T, int H, TOut* __restrict__ out) {
+  pdl_begin();
   const int nvec = H / 8;
   const int ntile = H / kTileN;
-  for (int t = blockIdx.x; t < T; t += gridDim.x) {
-    int slots[kTopK];
-    float w[kTopK];
+  const int per_block = kCombineThreads * kCombineVec;
+  const int chunks = (nvec + per_block - 1) / per_block;
+  const long work = static_cast<long>(T) * chunks;
+  for (long wi = blockIdx.x; wi < work; wi += gridDim.x) {
+    const int t = static_cast<int>(wi / chunks);
+    const int v0 = static_cast<int>(wi - static_cast<long>(t) * chunks) * per_block +
+                   threadIdx.x * kCombineVec;
+    const int4* ts = reinterpret_cast<const int4*>(token_slot + static_cast<size_t>(t) * kTopK);
+    const float4* tw = reinterpret_cast<const float4*>(token_weight + static_cast<size_t>(t) * kTopK);
+    const int4 s0 = __ldg(ts), s1 = __ldg(ts + 1);
+    const float4 w0 = __ldg(tw), w1 = __ldg(tw + 1);
+    const int slots[kTopK] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const float w[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    if (v0 >= nvec) continue;
+    const int tile = (v0 * 8) / kTileN;
+    float acc[kCombineVec][8];
+#pragma unroll
+    for (int k = 0; k < kCombineVec; ++k)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[k][i] = 0.0f;
+    // local picks occupy slots[0 .. nloc) in ascending expert order
 #pragma unroll
     for (int j = 0; j < kTopK; ++j) {
-      slots[j] = __ldg(token_slot + static_cast<size_t>(t) * kTopK + j);
-      w[j] = __ldg(token_weight + static_cast<size_t>(t) * kTopK + j);
-    }
-    for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
-      const int tile = (v * 8) / kTileN;
-      // issue every pick's load before reducing (local picks fill slots[0..nloc))
-      uint4 raw[kTopK];
-      float f[kTopK];
+      if (slots[j] < 0) break;
+      const size_t row = static_cast<size_t>(slots[j]);
+      const uint4* src = reinterpret_cast<const uint4*>(y + row * H) + v0;
+      uint4 raw[kCombineVec];
 #pragma unroll
-      for (int j = 0; j < kTopK; ++j) {
-        if (slots[j] >= 0) {
-          const size_t row = static_cast<size_t>(slots[j]);
-          raw[j] = __ldg(reinterpret_cast<const uint4*>(y + row * H) + v);
-          f[j] = __ldg(y_scale + row * ntile + tile) * w[j];
-        } else {
-          raw[j] = make_uint4(0, 0, 0, 0);
-          f[j] = 0.0f;
-        }
-      }
-      float acc[8];
+      for (int k = 0; k < kCombineVec; ++k) raw[k] = __ldg(src + k);
+      const float f = __ldg(y_scale + row * ntile + tile) * w[j];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-#pragma unroll
-      for (int j = 0; j < kTopK; ++j) {
-        const __half2* h = reinterpret_cast<const __half2*>(&raw[j]);
+      for (int k = 0; k < kCombineVec; ++k) {
+        const __half2* h = reinterpret_cast<const __half2*>(&raw[k]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const float2 q = __half22float2(h[i]);
-          acc[2 * i] = fmaf(f[j], q.x, acc[2 * i]);
-          acc[2 * i + 1] = fmaf(f[j], q.y, acc[2 * i + 1]);
+          acc[k][2 * i] = fmaf(f, q.x, acc[k][2 * i]);
+          acc[k][2 * i + 1] = fmaf(f, q.y, acc[k][2 * i + 1]);
         }
       }
-      store8(out + static_cast<size_t>(t) * H, v, acc);
     }
+#pragma unroll
+    for (int k = 0; k < kCombineVec; ++k) store8(out + static_cast<size_t>(t) * H, v0 + k, acc[k]);
   }
 }
 
@@ -629,15 +646,17 @@ cudaError_t launch_combine(const RunParams& p, cudaStream_t s) {
   if (p.T <= 0) return cudaSuccess;
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
-  int blocks = p.T < p.num_sms * 16 ? p.T : p.num_sms * 16;
+  const int per_block = kCombineThreads * kCombineVec;
+  const long work = static_cast<long>(p.T) * ((p.H / 8 + per_block - 1) / per_block);
+  const int blocks = static_cast<int>(work < p.num_sms * 16L ? work : p.num_sms * 16L);
   if (p.out_f32)
-    k_combine<float><<<blocks, 128, 0, s>>>(reinterpret_cast<const int32_t*>(ws + L.token_slot),
+    (void)launch_pdl(k_combine<float>, blocks, kCombineThreads, 0, s, reinterpret_cast<const int32_t*>(ws + L.token_slot),
                                             reinterpret_cast<const float*>(ws + L.token_weight),
                                             reinterpret_cast<const __half*>(ws + L.y_rows),
                                             reinterpret_cast<const float*>(ws + L.y_scale), p.T,
                                             p.H, static_cast<float*>(p.output));
   else
-    k_combine<__nv_bfloat16><<<blocks, 128, 0, s>>>(
+    (void)launch_pdl(k_combine<__nv_bfloat16>, blocks, kCombineThreads, 0, s,
         reinterpret_cast<const int32_t*>(ws + L.token_slot),
         reinterpret_cast<const float*>(ws + L.token_weight),
         reinterpret_cast<const __half*>(ws + L.y_rows),
