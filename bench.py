@@ -268,8 +268,9 @@ def run_sweep(device, weights, peaks):
         from oracle import routing as orouting  # routing ids for accounting only
         ids, _ = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), cfg.rsf)
         acc = call_accounting(ids, 0, 32, cfg.T)
-        time_calls(inp, weights, 0, cfg.rsf, 3)
-        ms, ph, _ = time_calls(inp, weights, 0, cfg.rsf, 10)
+        time_calls(inp, weights, 0, cfg.rsf, 3, phase=False)
+        ms, _, _ = time_calls(inp, weights, 0, cfg.rsf, 20, phase=False)  # no inter-kernel events
+        _, ph, _ = time_calls(inp, weights, 0, cfg.rsf, 10)                # phase breakdown
         us = ms * 1e3
         t_roof = max(acc["flops"] / (fp8_peak * 1e12), acc["bytes"] / (peaks["hbm_gbs"] * 1e9))
         rows.append({"config": name, "T": cfg.T, "P": acc["P"], "active_experts": acc["active_experts"],

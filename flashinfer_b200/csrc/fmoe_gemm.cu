@@ -185,13 +185,13 @@ __device__ __forceinline__ float swiglu(float up, float gate) {
   return __fdividef(up, 1.0f + __expf(-up)) * gate;
 }
 
-// Two-term e4m3 encoding of 16 values: x * inv = hi + lo with hi = e4m3(x * inv) and
-// lo = e4m3(x * inv - hi); one 16-byte store per term.
-__device__ __forceinline__ void encode_e4m3_2term16(const float* x, float inv, uint4* hi_dst,
-                                                    uint4* lo_dst) {
-  uint32_t hw[4], lw[4];
+// Two-term e4m3 encoding of 32 values: x * inv = hi + lo with hi = e4m3(x * inv) and
+// lo = e4m3(x * inv - hi); one 32-byte store (a full DRAM sector) per term.
+__device__ __forceinline__ void encode_e4m3_2term32(const float* x, float inv, uint8_t* hi_dst,
+                                                    uint8_t* lo_dst) {
+  uint32_t hw[8], lw[8];
 #pragma unroll
-  for (int w = 0; w < 4; ++w) {
+  for (int w = 0; w < 8; ++w) {
     uint32_t hbits = 0, lbits = 0;
 #pragma unroll
     for (int pr = 0; pr < 2; ++pr) {
@@ -206,20 +206,21 @@ __device__ __forceinline__ void encode_e4m3_2term16(const float* x, float inv, u
     hw[w] = hbits;
     lw[w] = lbits;
   }
-  *hi_dst = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-  *lo_dst = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  st_global_v8(hi_dst, hw);
+  st_global_v8(lo_dst, lw);
 }
 
-// 16 values times a power-of-two inv, rounded to fp16, stored as two 16-byte words.
-__device__ __forceinline__ void store_f16x16(const float* x, float inv, __half* dst) {
+// 16 values times a power-of-two inv, rounded to fp16, stored with one 32-byte store to
+// y[slot][col, col + 16) (a full DRAM sector per store).
+__device__ __forceinline__ void store_f16x16(const float* x, float inv, __half* y, size_t slot,
+                                             int col, int H) {
   uint32_t wv[8];
 #pragma unroll
   for (int w = 0; w < 8; ++w) {
     const __half2 pr = __floats2half2_rn(x[2 * w] * inv, x[2 * w + 1] * inv);
     wv[w] = *reinterpret_cast<const uint32_t*>(&pr);
   }
-  reinterpret_cast<uint4*>(dst)[0] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
-  reinterpret_cast<uint4*>(dst)[1] = make_uint4(wv[4], wv[5], wv[6], wv[7]);
+  st_global_v8(y + slot * static_cast<size_t>(H) + col, wv);
 }
 
 // Exponent k of the smallest 2^k with amax / 2^k <= 16384 (ceil(log2(amax)) - 14): the fp16
@@ -545,14 +546,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           amax = exchange_amax(tail, g, r, amax);
           if (valid) {
             const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
-            uint4* hi_dst =
-                reinterpret_cast<uint4*>(args.h_hi + row * args.I + u.n * kBlock + g * 64);
-            uint4* lo_dst =
-                reinterpret_cast<uint4*>(args.h_lo + row * args.I + u.n * kBlock + g * 64);
-            for (int cc = 0; cc < 4; ++cc) {
-              float h[16];
+            uint8_t* hi_dst = args.h_hi + row * args.I + u.n * kBlock + g * 64;
+            uint8_t* lo_dst = args.h_lo + row * args.I + u.n * kBlock + g * 64;
+            for (int cc = 0; cc < 4; cc += 2) {
+              float h[32];
               h16(cc, h);
-              encode_e4m3_2term16(h, inv, hi_dst + cc, lo_dst + cc);
+              h16(cc + 1, h + 16);
+              encode_e4m3_2term32(h, inv, hi_dst + cc * 16, lo_dst + cc * 16);
             }
             if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = amax / 448.0f;
           }
@@ -571,8 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int cc = 0; cc < 8; ++cc) {
               float v[16];
               split_sum16((cc >> 2) * 128 + g * 64 + (cc & 3) * 16, v);
-              store_f16x16(v, inv, args.y + row * args.H + u.n * kTileN + (cc >> 2) * 128 +
-                                       g * 64 + (cc & 3) * 16);
+              store_f16x16(v, inv, args.y, row,
+                           u.n * kTileN + (cc >> 2) * 128 + g * 64 + (cc & 3) * 16, args.H);
             }
             if (g == 0) args.y_scale[row * (args.H / kTileN) + u.n] = ldexpf(1.0f, k);
           }
@@ -597,11 +597,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         amax = exchange_amax(tail, g, r, amax);
         if (valid) {
           const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
-          uint4* hi_dst = reinterpret_cast<uint4*>(args.h_hi + row * args.I + u.n * kBlock + g * 64);
-          uint4* lo_dst = reinterpret_cast<uint4*>(args.h_lo + row * args.I + u.n * kBlock + g * 64);
+          uint8_t* hi_dst = args.h_hi + row * args.I + u.n * kBlock + g * 64;
+          uint8_t* lo_dst = args.h_lo + row * args.I + u.n * kBlock + g * 64;
 #pragma unroll
-          for (int cc = 0; cc < 4; ++cc)
-            encode_e4m3_2term16(acc + cc * 16, inv, hi_dst + cc, lo_dst + cc);
+          for (int cc = 0; cc < 2; ++cc)
+            encode_e4m3_2term32(acc + cc * 32, inv, hi_dst + cc * 32, lo_dst + cc * 32);
           if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = amax / 448.0f;
         }
       } else {
@@ -616,8 +616,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (valid) {
 #pragma unroll
           for (int cc = 0; cc < 8; ++cc)
-            store_f16x16(acc + cc * 16, inv, args.y + row * args.H + u.n * kTileN +
-                                                 (cc >> 2) * 128 + g * 64 + (cc & 3) * 16);
+            store_f16x16(acc + cc * 16, inv, args.y, row,
+                         u.n * kTileN + (cc >> 2) * 128 + g * 64 + (cc & 3) * 16, args.H);
           if (g == 0) args.y_scale[row * (args.H / kTileN) + u.n] = ldexpf(1.0f, k);
         }
       }

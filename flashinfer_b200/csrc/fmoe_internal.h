@@ -157,6 +157,20 @@ cudaError_t launch_route_permute(const void* logits, int logits_dtype, const voi
                                  int H, int I, int num_sms, const PermuteBuffers& b,
                                  cudaStream_t s);
 
+// ---------------------------------------------------------------- 256-bit global accesses
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&w)[8]) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(w[0]), "r"(w[1]),
+               "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+__device__ __forceinline__ void ld_global_nc_v8(const void* p, uint32_t (&w)[8]) {
+  asm volatile("ld.global.nc.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]), "=r"(w[4]), "=r"(w[5]),
+                 "=r"(w[6]), "=r"(w[7])
+               : "l"(p));
+}
+
 // ---------------------------------------------------------------- programmatic dependent launch
 // Every kernel of the path is launched with programmatic stream serialisation. A kernel first
 // lets the next kernel in the stream be scheduled (its CTAs are placed as resources free up and

@@ -581,9 +581,9 @@ __device__ __forceinline__ void store8(float* out, size_t v, const float (&acc)[
   o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
 }
 
-// Each thread owns kCombineVec consecutive 16-byte vectors (32 columns, inside one 256-column
-// scale tile) of one token's row: per local pick it issues all of that pick's loads at once, so
-// a thread keeps 64 bytes in flight; the picks are added in ascending expert order.
+// Each thread owns 32 consecutive output columns (inside one 256-column scale tile) of one
+// token: per local pick it issues both 32-byte loads of the y row at once (64 bytes in flight);
+// the picks are added in ascending expert order.
 constexpr int kCombineVec = 4;
 constexpr int kCombineThreads = 128;
 
@@ -610,7 +610,8 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(const int32_t* __re
     const int slots[kTopK] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
     const float w[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
     if (v0 >= nvec) continue;
-    const int tile = (v0 * 8) / kTileN;
+    const int col0 = v0 * 8;  // 32 columns: two 32-byte loads of the y row
+    const int tile = col0 / kTileN;
     float acc[kCombineVec][8];
 #pragma unroll
     for (int k = 0; k < kCombineVec; ++k)
@@ -621,17 +622,16 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(const int32_t* __re
     for (int j = 0; j < kTopK; ++j) {
       if (slots[j] < 0) break;
       const size_t row = static_cast<size_t>(slots[j]);
-      const uint4* src = reinterpret_cast<const uint4*>(y + row * H) + v0;
-      uint4 raw[kCombineVec];
-#pragma unroll
-      for (int k = 0; k < kCombineVec; ++k) raw[k] = __ldg(src + k);
+      uint32_t raw[2][8];
+      ld_global_nc_v8(y + row * H + col0, raw[0]);
+      ld_global_nc_v8(y + row * H + col0 + 16, raw[1]);
       const float f = __ldg(y_scale + row * ntile + tile) * w[j];
 #pragma unroll
       for (int k = 0; k < kCombineVec; ++k) {
-        const __half2* h = reinterpret_cast<const __half2*>(&raw[k]);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const float2 q = __half22float2(h[i]);
+          const uint32_t bits = raw[k >> 1][(k & 1) * 4 + i];
+          const float2 q = __half22float2(*reinterpret_cast<const __half2*>(&bits));
           acc[k][2 * i] = fmaf(f, q.x, acc[k][2 * i]);
           acc[k][2 * i + 1] = fmaf(f, q.y, acc[k][2 * i + 1]);
         }
