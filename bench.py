@@ -30,7 +30,13 @@ sys.path.insert(0, ROOT)
 from flashinfer_b200 import _lib, moe as fmoe, workload as wl  # noqa: E402
 
 METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
-KERNELS_PER_CALL = 7   # route+hist, scan, scatter, gather, gemm1, gemm2, combine
+SMALL_T = 32           # T <= SMALL_T: one fused route/plan/scatter kernel instead of three
+
+
+def kernels_per_call(T: int) -> int:
+    """Launches of one call: route+hist, scan, scatter (or the fused small-T plan kernel),
+    gather, gemm1, gemm2, combine."""
+    return 5 if T <= SMALL_T else 7
 
 
 def measured_peaks():
@@ -414,7 +420,7 @@ def main():
             "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms, 5)},
-            "gpu_launches": KERNELS_PER_CALL * args.steps,
+            "gpu_launches": kernels_per_call(cfg.T) * args.steps,
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_sweep:

@@ -249,10 +249,15 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
     return cudaEventRecord(static_cast<cudaEvent_t>(a->phase_events[i]), s) == cudaSuccess;
   };
   if (!mark(0)) return FMOE_ERR_CUDA;
-  // The scan kernel clears the status word before any GEMM can set it.
-  if (launch_route_hist(p, s) != cudaSuccess || launch_scan(p, s) != cudaSuccess || !mark(1))
-    return FMOE_ERR_CUDA;
-  if (launch_scatter_gather(p, s) != cudaSuccess || !mark(2)) return FMOE_ERR_CUDA;
+  // The plan kernel (k_scan or k_plan_small) clears the status word before any GEMM can set it.
+  if (T <= kSmallT) {
+    if (launch_plan_small(p, s) != cudaSuccess || !mark(1)) return FMOE_ERR_CUDA;
+    if (launch_gather(p, s) != cudaSuccess || !mark(2)) return FMOE_ERR_CUDA;
+  } else {
+    if (launch_route_hist(p, s) != cudaSuccess || launch_scan(p, s) != cudaSuccess || !mark(1))
+      return FMOE_ERR_CUDA;
+    if (launch_scatter_gather(p, s) != cudaSuccess || !mark(2)) return FMOE_ERR_CUDA;
+  }
   if (a->stop_after == FMOE_STOP_ROUTE || a->stop_after == FMOE_STOP_GATHER) return FMOE_OK;
 
   CUtensorMap tm_a, tm_w1, tm_hi, tm_lo, tm_w2, tm_sa1, tm_sa2;

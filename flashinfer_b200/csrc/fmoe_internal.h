@@ -127,6 +127,10 @@ cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias,
 cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s);
 cudaError_t launch_scan(const RunParams& p, cudaStream_t s);
 cudaError_t launch_scatter_gather(const RunParams& p, cudaStream_t s);
+cudaError_t launch_gather(const RunParams& p, cudaStream_t s);
+// T <= kSmallT: routing + histogram + plan + scatter in one CTA (replaces the three above)
+constexpr int kSmallT = 32;
+cudaError_t launch_plan_small(const RunParams& p, cudaStream_t s);
 cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUtensorMap& tm_w1,
                          const CUtensorMap& tm_sa, cudaStream_t s);
 cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,

@@ -42,10 +42,11 @@ __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, flo
 }
 
 // sigmoid with the same three roundings as 1/(1+exp(-x)) in fp32: exp(-x) correctly rounded
-// to fp32 (evaluated in double), then an IEEE fp32 add and an IEEE fp32 divide.
+// to fp32 (evaluated in double), then an IEEE fp32 add and an IEEE fp32 divide (1/y correctly
+// rounded, computed as the correctly rounded reciprocal).
 __device__ __forceinline__ float sigmoid_rn(float x) {
   const float e = static_cast<float>(exp(-static_cast<double>(x)));
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, e));
+  return __frcp_rn(__fadd_rn(1.0f, e));
 }
 
 // Routes one token with one warp. Returns, in every lane, the 8 picks (selection order:
@@ -83,20 +84,17 @@ __device__ __forceinline__ void route_token(const TL* __restrict__ row, const fl
     m1 = n1;
     m2 = n2;
   }
-  const float gscore = __fadd_rn(m1, m2);
-  float gs[kGroups];
+  const float gscore = __fadd_rn(m1, m2);  // the same in the 4 lanes of a group
+  // Keep the 4 best groups; ties go to the lower group index (kernel.py:418-426). Each lane
+  // ranks its own group against the 8 group scores.
+  const int myg = lane >> 2;
+  int grank = 0;
 #pragma unroll
-  for (int g = 0; g < kGroups; ++g) gs[g] = __shfl_sync(0xffffffffu, gscore, 4 * g);
-  // Keep the 4 best groups; ties go to the lower group index (kernel.py:418-426).
-  uint32_t gmask = 0;
-#pragma unroll
-  for (int g = 0; g < kGroups; ++g) {
-    int rank = 0;
-#pragma unroll
-    for (int h = 0; h < kGroups; ++h) rank += (gs[h] > gs[g]) || (gs[h] == gs[g] && h < g);
-    if (rank < kTopKGroups) gmask |= 1u << g;
+  for (int h = 0; h < kGroups; ++h) {
+    const float gh = __shfl_sync(0xffffffffu, gscore, 4 * h);
+    grank += (gh > gscore) || (gh == gscore && h < myg);
   }
-  const bool kept = (gmask >> (lane >> 2)) & 1u;
+  const bool kept = grank < kTopKGroups;
   // Top-8 over the kept groups by biased score; ties to the lowest index (kernel.py:428-438).
   // Each candidate becomes an order-preserving 32-bit key, so one warp-wide max reduction
   // (redux.sync) finds the best score and a second one the lowest index holding it.
@@ -135,13 +133,18 @@ __device__ __forceinline__ void route_token(const TL* __restrict__ row, const fl
     }
   }
   // Weights from the un-biased scores (moe.py:165-168): (s / (sum + 1e-20)) * rsf, with the
-  // sum taken in selection order.
+  // sum taken in selection order; lane k divides pick k, then every lane gathers the eight.
   float denom = 0.0f;
+  float my_sv = sv[0];
 #pragma unroll
-  for (int k = 0; k < kTopK; ++k) denom = __fadd_rn(denom, sv[k]);
+  for (int k = 0; k < kTopK; ++k) {
+    denom = __fadd_rn(denom, sv[k]);
+    if (lane == k) my_sv = sv[k];
+  }
   denom = __fadd_rn(denom, 1e-20f);
+  const float my_w = __fmul_rn(__fdiv_rn(my_sv, denom), rsf);
 #pragma unroll
-  for (int k = 0; k < kTopK; ++k) wts[k] = __fmul_rn(__fdiv_rn(sv[k], denom), rsf);
+  for (int k = 0; k < kTopK; ++k) wts[k] = __shfl_sync(0xffffffffu, my_w, k);
 }
 
 __device__ __forceinline__ void store_picks(int32_t* ids_out, float* w_out, int t,
@@ -266,6 +269,34 @@ __device__ int choose_split(int tiles, int nkb, int G) {
   return best;
 }
 
+// Expert bases padded to 128 slots and the GEMM work plan from the per-expert counts (one
+// thread); also clears the status word before any GEMM can set it.
+__device__ void write_plan(const int* cnt, int E, int H, int I, int G, int* base, int32_t* plan,
+                           int32_t* status) {
+  int acc = 0, pairs = 0;
+  for (int e = 0; e < E; ++e) {
+    base[e] = acc;
+    acc += (cnt[e] + kTileM - 1) / kTileM * kTileM;
+    pairs += cnt[e];
+  }
+  base[E] = acc;
+  const int mtiles = acc / kTileM;
+  const int tiles1 = mtiles * (I / kBlock);
+  const int tiles2 = mtiles * (H / kTileN);
+  const int s1 = choose_split(tiles1, H / kBlock, G);
+  const int s2 = choose_split(tiles2, I / kBlock, G);
+  plan[kPlanPairs] = pairs;
+  plan[kPlanPadded] = acc;
+  plan[kPlanMTiles] = mtiles;
+  plan[kPlanSplit1] = s1;
+  plan[kPlanUnits1] = tiles1 * s1;
+  plan[kPlanSplit2] = s2;
+  plan[kPlanUnits2] = tiles2 * s2;
+  plan[kPlanTiles1] = tiles1;
+  plan[kPlanTiles2] = tiles2;
+  status[0] = 0;
+}
+
 __global__ void __launch_bounds__(1024) k_scan(const int32_t* __restrict__ block_hist,
                                                int nblocks, int E, int H, int I, int G,
                                                int32_t* __restrict__ block_off,
@@ -300,30 +331,7 @@ __global__ void __launch_bounds__(1024) k_scan(const int32_t* __restrict__ block
     if (lane == 0) cnt[e] = run;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0, pairs = 0;
-    for (int e = 0; e < E; ++e) {
-      base[e] = acc;
-      acc += (cnt[e] + kTileM - 1) / kTileM * kTileM;
-      pairs += cnt[e];
-    }
-    base[E] = acc;
-    const int mtiles = acc / kTileM;
-    const int tiles1 = mtiles * (I / kBlock);
-    const int tiles2 = mtiles * (H / kTileN);
-    const int s1 = choose_split(tiles1, H / kBlock, G);
-    const int s2 = choose_split(tiles2, I / kBlock, G);
-    plan[kPlanPairs] = pairs;
-    plan[kPlanPadded] = acc;
-    plan[kPlanMTiles] = mtiles;
-    plan[kPlanSplit1] = s1;
-    plan[kPlanUnits1] = tiles1 * s1;
-    plan[kPlanSplit2] = s2;
-    plan[kPlanUnits2] = tiles2 * s2;
-    plan[kPlanTiles1] = tiles1;
-    plan[kPlanTiles2] = tiles2;
-    status[0] = 0;
-  }
+  if (threadIdx.x == 0) write_plan(cnt, E, H, I, G, base, plan, status);
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     expert_count[e] = cnt[e];
@@ -436,6 +444,120 @@ __global__ void __launch_bounds__(256) k_scatter(
   }
 }
 
+// Small batches (T <= kSmallT): routing, the histogram, the plan and the scatter in one CTA,
+// replacing k_route_hist + k_scan + k_scatter (three dependent launches of a few tokens each).
+// Same results: the plan comes from write_plan, a token's slot rank for expert e is the number
+// of earlier tokens that picked e (stable, tokens ascending; a popcount of the expert's token
+// mask), its picks are listed by ascending
+// expert, and padding slots are marked empty.
+template <typename TL, typename TB>
+__global__ void __launch_bounds__(1024) k_plan_small(
+    const TL* __restrict__ logits, const TB* __restrict__ bias, int T, float rsf, int local_start,
+    int E, int H, int I, int G, int32_t* __restrict__ ids_out, float* __restrict__ w_out,
+    int32_t* __restrict__ plan, int32_t* __restrict__ expert_count,
+    int32_t* __restrict__ expert_base, int32_t* __restrict__ counters,
+    int32_t* __restrict__ status, int32_t* __restrict__ slot_token,
+    float* __restrict__ slot_weight, int32_t* __restrict__ token_slot,
+    float* __restrict__ token_weight) {
+  __shared__ int cnt[kMaxLocalExperts];
+  __shared__ int base[kMaxLocalExperts + 1];
+  __shared__ int ids_s[kSmallT][kTopK];
+  __shared__ uint32_t tokmask[kMaxLocalExperts][kSmallT / 32];  // tokens that picked expert e
+  pdl_begin();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    cnt[e] = 0;
+#pragma unroll
+    for (int wd = 0; wd < kSmallT / 32; ++wd) tokmask[e][wd] = 0u;
+  }
+  __syncthreads();
+  float b[8];
+  load8<TB>(bias + lane * 8, b);
+  for (int t = warp; t < T; t += nwarp) {
+    int ids[kTopK];
+    float w[kTopK];
+    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, lane, ids, w);
+    if (lane == 0) {
+      store_picks(ids_out, w_out, t, ids, w);
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) ids_s[t][k] = ids[k];
+    }
+    if (lane < kTopK) {
+      int mine = ids[0];
+#pragma unroll
+      for (int k = 1; k < kTopK; ++k)
+        if (lane == k) mine = ids[k];
+      const int le = mine - local_start;
+      if (le >= 0 && le < E) {
+        atomicAdd(&cnt[le], 1);
+        atomicOr(&tokmask[le][t >> 5], 1u << (t & 31));
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) write_plan(cnt, E, H, I, G, base, plan, status);
+  // token t (thread t): its local picks in ascending expert order
+  const int t = threadIdx.x;
+  int le[kTopK];
+  float lw[kTopK];
+  int nloc = 0;
+  if (t < T) {
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      const int e = ids_s[t][k] - local_start;
+      if (e >= 0 && e < E) {
+        const float w = w_out[static_cast<size_t>(t) * kTopK + k];
+        int j = nloc;  // insertion into the ascending list le[0..nloc)
+        while (j > 0 && le[j - 1] > e) {
+          le[j] = le[j - 1];
+          lw[j] = lw[j - 1];
+          --j;
+        }
+        le[j] = e;
+        lw[j] = w;
+        ++nloc;
+      }
+    }
+  }
+  __syncthreads();  // base[] is visible
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    expert_count[e] = cnt[e];
+    expert_base[e] = base[e];
+  }
+  if (threadIdx.x == 0) expert_base[E] = base[E];
+  for (int i = threadIdx.x; i < 2 * kMaxSplitUnits; i += blockDim.x) counters[i] = 0;
+  if (t < T) {
+    int* ts = token_slot + static_cast<size_t>(t) * kTopK;
+    float* tw = token_weight + static_cast<size_t>(t) * kTopK;
+    for (int j = 0; j < kTopK; ++j) {
+      if (j < nloc) {
+        const int e = le[j];
+        // rank among the tokens that picked e = earlier tokens in its token mask
+        int rank = 0;
+#pragma unroll
+        for (int wd = 0; wd < kSmallT / 32; ++wd) {
+          const int lo = wd * 32;
+          const uint32_t below = t >= lo + 32 ? 0xffffffffu : (t <= lo ? 0u : (1u << (t - lo)) - 1u);
+          rank += __popc(tokmask[e][wd] & below);
+        }
+        const int slot = base[e] + rank;
+        slot_token[slot] = t;
+        slot_weight[slot] = lw[j];
+        ts[j] = slot;
+        tw[j] = lw[j];
+      } else {
+        ts[j] = -1;
+        tw[j] = 0.0f;
+      }
+    }
+  }
+  for (int e = warp; e < E; e += nwarp)
+    for (int sl = base[e] + cnt[e] + lane; sl < base[e + 1]; sl += 32) {
+      slot_token[sl] = -1;
+      slot_weight[sl] = 0.0f;
+    }
+}
+
 // Gather: one warp per token reads the token's e4m3 row once (7168 B = 14 x 16 B per lane)
 // and writes it, with its 128-column scales, to each of the token's slots.
 __global__ void __launch_bounds__(256) k_gather_tokens(const int32_t* __restrict__ token_slot,
@@ -526,12 +648,42 @@ cudaError_t launch_scatter_gather(const RunParams& p, cudaStream_t s) {
       reinterpret_cast<float*>(ws + L.token_weight));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
+  return launch_gather(p, s);
+}
+
+cudaError_t launch_gather(const RunParams& p, cudaStream_t s) {
+  if (p.T <= 0) return cudaSuccess;
+  uint8_t* ws = p.ws;
+  const Layout& L = p.L;
   int blocks = (p.T + 7) / 8;
   if (blocks > p.num_sms * 8) blocks = p.num_sms * 8;
   (void)launch_pdl(k_gather_tokens, blocks, 256, 0, s, reinterpret_cast<const int32_t*>(ws + L.token_slot),
                                          p.hidden, p.hidden_scale, p.T, p.H, L.cap,
                                          ws + L.a_perm, reinterpret_cast<float*>(ws + L.a_scale_t));
   return cudaGetLastError();
+}
+
+cudaError_t launch_plan_small(const RunParams& p, cudaStream_t s) {
+  if (p.T <= 0) return cudaSuccess;
+  uint8_t* ws = p.ws;
+  const Layout& L = p.L;
+  return dispatch_dtypes(p.logits_dtype, p.bias_dtype, [&](auto tl, auto tb) {
+    using TL = decltype(tl);
+    using TB = decltype(tb);
+    (void)launch_pdl(k_plan_small<TL, TB>, 1, 1024, 0, s, static_cast<const TL*>(p.logits),
+                     static_cast<const TB*>(p.bias), p.T, p.rsf, p.local_start, p.E, p.H, p.I,
+                     p.num_sms, reinterpret_cast<int32_t*>(ws + L.topk_ids),
+                     reinterpret_cast<float*>(ws + L.topk_w), reinterpret_cast<int32_t*>(ws + L.plan),
+                     reinterpret_cast<int32_t*>(ws + L.expert_count),
+                     reinterpret_cast<int32_t*>(ws + L.expert_base),
+                     reinterpret_cast<int32_t*>(ws + L.counters),
+                     reinterpret_cast<int32_t*>(ws + L.status),
+                     reinterpret_cast<int32_t*>(ws + L.slot_token),
+                     reinterpret_cast<float*>(ws + L.slot_weight),
+                     reinterpret_cast<int32_t*>(ws + L.token_slot),
+                     reinterpret_cast<float*>(ws + L.token_weight));
+    return cudaGetLastError();
+  });
 }
 
 cudaError_t launch_route_permute(const void* logits, int logits_dtype, const void* bias,
