@@ -147,6 +147,18 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
   }
 }
 
+// The same for a thread that is not on the critical path (the TMA producers): each poll may
+// park the thread for up to 2 us, leaving its issue slots to the epilogue warps.
+__device__ __forceinline__ bool wait_or_abort_parked(uint64_t* bar, uint32_t parity,
+                                                     volatile int* abort_flag) {
+  const uint64_t t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > FMOE_WAIT_NS) return false;
+  }
+}
+
 __device__ __forceinline__ void raise_abort(GemmTail* tail, int32_t* status, int code) {
   *reinterpret_cast<volatile int*>(&tail->abort_flag) = 1;
   atomicOr(status, code);
@@ -310,7 +322,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // This producer issued iteration it - 2 after the release of it - 2 - NS, and the MMA
           // warp releases in order, so round r - 2 of this stage is already released: the empty
           // barrier is at most one phase behind and the parity wait is unambiguous.
-          if (r > 0 && !wait_or_abort(&tail->empty[s], (r & 1) ^ 1, abort_flag)) {
+          if (r > 0 && !wait_or_abort_parked(&tail->empty[s], (r & 1) ^ 1, abort_flag)) {
             raise_abort(tail, args.status, kErr);
             ok = false;
             break;

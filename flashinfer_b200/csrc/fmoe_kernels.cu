@@ -311,7 +311,21 @@ __global__ void __launch_bounds__(1024) k_scan(const int32_t* __restrict__ block
   pdl_begin();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
   const int n = nblocks * E;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) sh[i] = block_hist[i];
+  {
+    // all of a thread's loads in flight at once (the scan runs as a single CTA)
+    constexpr int kPer = kMaxBlockCounts / 1024;
+    int v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = threadIdx.x + j * 1024;
+      v[j] = i < n ? __ldg(block_hist + i) : 0;
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int i = threadIdx.x + j * 1024;
+      if (i < n) sh[i] = v[j];
+    }
+  }
   __syncthreads();
   // warp w scans experts w, w+32, ...: exclusive prefix over blocks, 32 blocks per step
   for (int e = warp; e < E; e += nwarp) {
