@@ -30,13 +30,14 @@ sys.path.insert(0, ROOT)
 from flashinfer_b200 import _lib, moe as fmoe, workload as wl  # noqa: E402
 
 METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
-SMALL_T = 32           # T <= SMALL_T: one fused route/plan/scatter kernel instead of three
+SMALL_T = 32           # T <= SMALL_T: fused route/plan/scatter kernel, split-K finish kernels
 
 
 def kernels_per_call(T: int) -> int:
-    """Launches of one call: route+hist, scan, scatter (or the fused small-T plan kernel),
-    gather, gemm1, gemm2, combine."""
-    return 5 if T <= SMALL_T else 7
+    """Launches of one call: route+hist, scan, scatter, gather, gemm1, gemm2, combine; for
+    T <= SMALL_T the fused plan kernel replaces the first three and a split-K finish kernel
+    follows each GEMM."""
+    return 7
 
 
 def measured_peaks():

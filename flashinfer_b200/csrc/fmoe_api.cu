@@ -271,10 +271,13 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
       !make_tmap_f32_rows(&tm_sa2, p.ws + L.h_scale_t, L.cap, I / kBlock, 128))
     return FMOE_ERR_CUDA;
 
-  if (launch_gemm1(p, tm_a, tm_w1, tm_sa1, s) != cudaSuccess || !mark(3)) return FMOE_ERR_CUDA;
+  if (launch_gemm1(p, tm_a, tm_w1, tm_sa1, s) != cudaSuccess) return FMOE_ERR_CUDA;
+  if (T <= kSplitMaxT && launch_split_finish(p, 1, s) != cudaSuccess) return FMOE_ERR_CUDA;
+  if (!mark(3)) return FMOE_ERR_CUDA;
   if (a->stop_after == FMOE_STOP_GEMM1) return FMOE_OK;
-  if (launch_gemm2(p, tm_hi, tm_lo, tm_w2, tm_sa2, s) != cudaSuccess || !mark(4))
-    return FMOE_ERR_CUDA;
+  if (launch_gemm2(p, tm_hi, tm_lo, tm_w2, tm_sa2, s) != cudaSuccess) return FMOE_ERR_CUDA;
+  if (T <= kSplitMaxT && launch_split_finish(p, 2, s) != cudaSuccess) return FMOE_ERR_CUDA;
+  if (!mark(4)) return FMOE_ERR_CUDA;
   if (a->stop_after == FMOE_STOP_GEMM2) return FMOE_OK;
   if (launch_combine(p, s) != cudaSuccess || !mark(5)) return FMOE_ERR_CUDA;
   return FMOE_OK;

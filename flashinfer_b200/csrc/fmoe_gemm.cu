@@ -19,10 +19,10 @@
 //               with packed FMA (the reference's "partial * sa * sb" promotion,
 //               kernel.py:167-171).
 // Work unit = (tile, K split). Tiles are ordered expert -> n-tile -> m-tile so concurrently
-// running CTAs share weight tiles in L2. When there are fewer tiles than SMs, the K range is
-// split; every split writes its partial tile, and the last one to arrive (an atomic counter)
-// sums them in split order and runs the epilogue -- deterministic, and no CTA ever waits on
-// another.
+// running CTAs share weight tiles in L2. For small batches with fewer tiles than SMs the K range
+// is split; every split writes its fp32 partial tile and k_split_finish (a separate kernel,
+// one CTA per tile) sums them in split order and runs the epilogue -- deterministic, and no CTA
+// ever waits on another.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -493,14 +493,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool valid = r < u.nrows;
       const size_t row = static_cast<size_t>(u.row0) + r;
       if (S > 1) {
-        // split-K: publish this split's partial tile; the last arriver sums the splits in split
-        // order and runs the epilogue straight from the partials, 16 columns at a time (the
-        // accumulators are dead on this path, which keeps it from adding register pressure
-        // to the main one)
-        const int tile = unit / S;
-        const int slot_rows = args.partial_rows;
+        // split-K: publish this split's partial tile (valid rows); k_split_finish sums the
+        // splits of each tile in split order and runs the epilogue
         if (valid) {
-          float* p = args.partials + (static_cast<size_t>(unit) * slot_rows + r) * kTileN;
+          float* p = args.partials + (static_cast<size_t>(unit) * args.partial_rows + r) * kTileN;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             float4* dst = reinterpret_cast<float4*>(p + h * 128 + g * 64);
@@ -508,85 +504,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 16; ++i)
               dst[i] = make_float4(acc[h * 64 + 4 * i], acc[h * 64 + 4 * i + 1],
                                    acc[h * 64 + 4 * i + 2], acc[h * 64 + 4 * i + 3]);
-          }
-        }
-        __threadfence();
-        named_bar_sync(1, kEpiWarps * 32);
-        if (etid == 0) {
-          const int old = atomicAdd(args.counters + (KIND == 1 ? 0 : kMaxSplitUnits) + tile, 1);
-          tail->last_flag = (old == S - 1);
-        }
-        named_bar_sync(1, kEpiWarps * 32);
-        if (!tail->last_flag) continue;
-        __threadfence();
-        const float* p0 = args.partials + (static_cast<size_t>(tile * S) * slot_rows + r) * kTileN;
-        const size_t split_stride = static_cast<size_t>(slot_rows) * kTileN;
-        // columns [col, col + 16) of this thread's row, summed over the splits in split order
-        auto split_sum16 = [&](int col, float* v) {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) v[i] = 0.0f;
-          if (!valid) return;
-          for (int sp = 0; sp < S; ++sp) {
-            const float4* src = reinterpret_cast<const float4*>(p0 + sp * split_stride + col);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float4 x = __ldcg(src + i);
-              v[4 * i] += x.x;
-              v[4 * i + 1] += x.y;
-              v[4 * i + 2] += x.z;
-              v[4 * i + 3] += x.w;
-            }
-          }
-        };
-        if (KIND == 1) {
-          auto h16 = [&](int cc, float* h) {
-            float gate[16];
-            split_sum16(g * 64 + cc * 16, gate);
-            split_sum16(128 + g * 64 + cc * 16, h);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) h[i] = swiglu(h[i], gate[i]);
-          };
-          float amax = 0.0f;
-          if (valid) {
-            for (int cc = 0; cc < 4; ++cc) {
-              float h[16];
-              h16(cc, h);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(h[i]));
-            }
-          }
-          amax = exchange_amax(tail, g, r, amax);
-          if (valid) {
-            const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
-            uint8_t* hi_dst = args.h_hi + row * args.I + u.n * kBlock + g * 64;
-            uint8_t* lo_dst = args.h_lo + row * args.I + u.n * kBlock + g * 64;
-            for (int cc = 0; cc < 4; cc += 2) {
-              float h[32];
-              h16(cc, h);
-              h16(cc + 1, h + 16);
-              encode_e4m3_2term32(h, inv, hi_dst + cc * 16, lo_dst + cc * 16);
-            }
-            if (g == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + row] = amax / 448.0f;
-          }
-        } else {
-          float amax = 0.0f;
-          for (int cc = 0; cc < 8; ++cc) {
-            float v[16];
-            split_sum16((cc >> 2) * 128 + g * 64 + (cc & 3) * 16, v);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
-          }
-          amax = exchange_amax(tail, g, r, amax);
-          const int k = pow2_exponent_for_f16(amax);
-          const float inv = ldexpf(1.0f, -k);
-          if (valid) {
-            for (int cc = 0; cc < 8; ++cc) {
-              float v[16];
-              split_sum16((cc >> 2) * 128 + g * 64 + (cc & 3) * 16, v);
-              store_f16x16(v, inv, args.y, row,
-                           u.n * kTileN + (cc >> 2) * 128 + g * 64 + (cc & 3) * 16, args.H);
-            }
-            if (g == 0) args.y_scale[row * (args.H / kTileN) + u.n] = ldexpf(1.0f, k);
           }
         }
         continue;
@@ -645,20 +562,115 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Split-K finish (small batches): one CTA per tile sums the tile's S partial tiles in split
+// order into shared memory -- every thread takes (row, 4-column) items and keeps four splits'
+// loads in flight -- then runs the tile's epilogue with one warp per valid row: SwiGLU and the
+// two-term e4m3 encoding (KIND 1) or fp16 with a power-of-two scale (KIND 2), the same
+// arithmetic as k_gemm's register epilogue.
 template <int KIND>
-static cudaError_t launch_gemm_kind(const RunParams& p, const CUtensorMap& a0,
-                                    const CUtensorMap& a1, const CUtensorMap& w,
-                                    const CUtensorMap& sa, cudaStream_t s) {
-  const size_t smem = gemm_smem_bytes<KIND>();
-  static int configured_device = -1;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
-    cudaError_t e = cudaFuncSetAttribute(k_gemm<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-    configured_device = dev;
+__global__ void __launch_bounds__(256) k_split_finish(const GemmArgs args) {
+  pdl_begin();
+  const int S = args.plan[KIND == 1 ? kPlanSplit1 : kPlanSplit2];
+  if (S <= 1) return;
+  const int tiles = args.plan[KIND == 1 ? kPlanTiles1 : kPlanTiles2];
+  __shared__ int ebase[kMaxLocalExperts + 1];
+  __shared__ int ecnt[kMaxLocalExperts];
+  extern __shared__ float red[];  // [partial_rows][kTileN]
+  const int E = args.E;
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) {
+    ebase[i] = args.expert_base[i];
+    if (i < E) ecnt[i] = args.expert_count[i];
   }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarp = blockDim.x >> 5;
+  const int nkb = KIND == 1 ? args.H / kBlock : args.I / kBlock;
+  const int NT = KIND == 1 ? args.I / kBlock : args.H / kTileN;
+  const size_t split_stride = static_cast<size_t>(args.partial_rows) * kTileN;
+  for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    const Unit u = decode_unit(tile * S, S, NT, nkb, ebase, ecnt, E);
+    const float* tile0 = args.partials + static_cast<size_t>(tile * S) * split_stride;
+    for (int item = threadIdx.x; item < u.nrows * (kTileN / 4); item += blockDim.x) {
+      const int rr = item / (kTileN / 4);
+      const int c4 = (item - rr * (kTileN / 4)) * 4;
+      const float* src = tile0 + static_cast<size_t>(rr) * kTileN + c4;
+      float4 sum = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int sp0 = 0; sp0 < S; sp0 += 4) {
+        float4 x[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (sp0 + j < S) x[j] = __ldcg(reinterpret_cast<const float4*>(src + (sp0 + j) * split_stride));
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if (sp0 + j < S) {
+            sum.x += x[j].x;
+            sum.y += x[j].y;
+            sum.z += x[j].z;
+            sum.w += x[j].w;
+          }
+        }
+      }
+      *reinterpret_cast<float4*>(red + rr * kTileN + c4) = sum;
+    }
+    __syncthreads();
+    for (int rr = warp; rr < u.nrows; rr += nwarp) {
+      const size_t row = static_cast<size_t>(u.row0) + rr;
+      const float* v = red + rr * kTileN;
+      if (KIND == 1) {
+        // lane: intermediate columns lane*4 + [0,4) of the tile's 128 (gate | up halves)
+        float h[4];
+        float m = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          h[j] = swiglu(v[128 + lane * 4 + j], v[lane * 4 + j]);
+          m = fmaxf(m, fabsf(h[j]));
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        const float inv = m > 0.0f ? 448.0f / m : 0.0f;
+        uint32_t hw = 0, lw = 0;
+#pragma unroll
+        for (int pr = 0; pr < 2; ++pr) {
+          const float x0 = h[2 * pr] * inv, x1 = h[2 * pr + 1] * inv;
+          const uint16_t hp = pack_e4m3x2(x0, x1);
+          const float2 back = unpack_e4m3x2(hp);
+          const uint16_t lp = pack_e4m3x2(x0 - back.x, x1 - back.y);
+          hw |= static_cast<uint32_t>(hp) << (16 * pr);
+          lw |= static_cast<uint32_t>(lp) << (16 * pr);
+        }
+        const size_t off = row * args.I + static_cast<size_t>(u.n) * kBlock + lane * 4;
+        *reinterpret_cast<uint32_t*>(args.h_hi + off) = hw;
+        *reinterpret_cast<uint32_t*>(args.h_lo + off) = lw;
+        if (lane == 0) args.h_scale_t[static_cast<size_t>(u.n) * args.cap + row] = m / 448.0f;
+      } else {
+        // lane: output columns lane*8 + [0,8) of the tile's 256
+        float x[8];
+        float m = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          x[j] = v[lane * 8 + j];
+          m = fmaxf(m, fabsf(x[j]));
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        const int k = pow2_exponent_for_f16(m);
+        const float inv = ldexpf(1.0f, -k);
+        uint32_t wv[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const __half2 pr = __floats2half2_rn(x[2 * w] * inv, x[2 * w + 1] * inv);
+          wv[w] = *reinterpret_cast<const uint32_t*>(&pr);
+        }
+        *reinterpret_cast<uint4*>(args.y + row * args.H + static_cast<size_t>(u.n) * kTileN +
+                                  lane * 8) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+        if (lane == 0) args.y_scale[row * (args.H / kTileN) + u.n] = ldexpf(1.0f, k);
+      }
+    }
+    __syncthreads();  // red is rewritten by the next tile
+  }
+}
+
+template <int KIND>
+static GemmArgs gemm_args(const RunParams& p) {
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
   GemmArgs a{};
@@ -680,7 +692,35 @@ static cudaError_t launch_gemm_kind(const RunParams& p, const CUtensorMap& a0,
   a.I = p.I;
   a.cap = L.cap;
   a.partial_rows = static_cast<int>(L.partial_rows);
+  return a;
+}
+
+template <int KIND>
+static cudaError_t launch_gemm_kind(const RunParams& p, const CUtensorMap& a0,
+                                    const CUtensorMap& a1, const CUtensorMap& w,
+                                    const CUtensorMap& sa, cudaStream_t s) {
+  const size_t smem = gemm_smem_bytes<KIND>();
+  static int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaError_t e = cudaFuncSetAttribute(k_gemm<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  const GemmArgs a = gemm_args<KIND>(p);
   (void)launch_pdl(k_gemm<KIND>, p.num_sms, kThreads, smem, s, a0, a1, w, sa, a);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_finish(const RunParams& p, int kind, cudaStream_t s) {
+  // at most partial_rows (<= kSplitMaxT) rows of 256 fp32 per tile in shared memory
+  const size_t smem = static_cast<size_t>(p.L.partial_rows) * kTileN * 4;
+  if (kind == 1)
+    (void)launch_pdl(k_split_finish<1>, p.num_sms, 256, smem, s, gemm_args<1>(p));
+  else
+    (void)launch_pdl(k_split_finish<2>, p.num_sms, 256, smem, s, gemm_args<2>(p));
   return cudaGetLastError();
 }
 

@@ -128,6 +128,10 @@ cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s);
 cudaError_t launch_scan(const RunParams& p, cudaStream_t s);
 cudaError_t launch_scatter_gather(const RunParams& p, cudaStream_t s);
 cudaError_t launch_gather(const RunParams& p, cudaStream_t s);
+// Split-K (GEMM units over K ranges) only for T <= kSplitMaxT, where a call has fewer tiles than
+// SMs; the split partial tiles are finished by launch_split_finish(kind) after each GEMM.
+constexpr int kSplitMaxT = 32;
+cudaError_t launch_split_finish(const RunParams& p, int kind, cudaStream_t s);
 // T <= kSmallT: routing + histogram + plan + scatter in one CTA (replaces the three above)
 constexpr int kSmallT = 32;
 cudaError_t launch_plan_small(const RunParams& p, cudaStream_t s);

@@ -252,8 +252,8 @@ cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias,
 // K splits per tile for a persistent grid of G CTAs, used only when there are fewer tiles than
 // CTAs (split units cost a partial-tile round trip and a fence each). Cost, in K blocks on the
 // busiest CTA: waves * ceil(nkb / s) plus per-unit overheads. Ties keep the smaller split.
-__device__ int choose_split(int tiles, int nkb, int G) {
-  if (tiles <= 0 || tiles >= G) return 1;
+__device__ int choose_split(int tiles, int nkb, int G, int allow) {
+  if (!allow || tiles <= 0 || tiles >= G) return 1;
   int best = 1;
   long best_cost = 0x7fffffffffffL;
   for (int s = 1; s <= kMaxSplit && s <= nkb; ++s) {
@@ -271,8 +271,8 @@ __device__ int choose_split(int tiles, int nkb, int G) {
 
 // Expert bases padded to 128 slots and the GEMM work plan from the per-expert counts (one
 // thread); also clears the status word before any GEMM can set it.
-__device__ void write_plan(const int* cnt, int E, int H, int I, int G, int* base, int32_t* plan,
-                           int32_t* status) {
+__device__ void write_plan(const int* cnt, int E, int H, int I, int G, int allow_split, int* base,
+                           int32_t* plan, int32_t* status) {
   int acc = 0, pairs = 0;
   for (int e = 0; e < E; ++e) {
     base[e] = acc;
@@ -283,8 +283,8 @@ __device__ void write_plan(const int* cnt, int E, int H, int I, int G, int* base
   const int mtiles = acc / kTileM;
   const int tiles1 = mtiles * (I / kBlock);
   const int tiles2 = mtiles * (H / kTileN);
-  const int s1 = choose_split(tiles1, H / kBlock, G);
-  const int s2 = choose_split(tiles2, I / kBlock, G);
+  const int s1 = choose_split(tiles1, H / kBlock, G, allow_split);
+  const int s2 = choose_split(tiles2, I / kBlock, G, allow_split);
   plan[kPlanPairs] = pairs;
   plan[kPlanPadded] = acc;
   plan[kPlanMTiles] = mtiles;
@@ -299,6 +299,7 @@ __device__ void write_plan(const int* cnt, int E, int H, int I, int G, int* base
 
 __global__ void __launch_bounds__(1024) k_scan(const int32_t* __restrict__ block_hist,
                                                int nblocks, int E, int H, int I, int G,
+                                               int allow_split,
                                                int32_t* __restrict__ block_off,
                                                int32_t* __restrict__ plan,
                                                int32_t* __restrict__ expert_count,
@@ -345,7 +346,7 @@ __global__ void __launch_bounds__(1024) k_scan(const int32_t* __restrict__ block
     if (lane == 0) cnt[e] = run;
   }
   __syncthreads();
-  if (threadIdx.x == 0) write_plan(cnt, E, H, I, G, base, plan, status);
+  if (threadIdx.x == 0) write_plan(cnt, E, H, I, G, allow_split, base, plan, status);
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     expert_count[e] = cnt[e];
@@ -509,7 +510,7 @@ __global__ void __launch_bounds__(1024) k_plan_small(
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) write_plan(cnt, E, H, I, G, base, plan, status);
+  if (threadIdx.x == 0) write_plan(cnt, E, H, I, G, 1, base, plan, status);
   // token t (thread t): its local picks in ascending expert order
   const int t = threadIdx.x;
   int le[kTopK];
@@ -638,7 +639,8 @@ cudaError_t launch_scan(const RunParams& p, cudaStream_t s) {
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
   (void)launch_pdl(k_scan, 1, 1024, 0, s, reinterpret_cast<const int32_t*>(ws + L.block_hist), L.nblocks, p.E,
-                            p.H, p.I, p.num_sms, reinterpret_cast<int32_t*>(ws + L.block_off),
+                            p.H, p.I, p.num_sms, p.T <= kSplitMaxT ? 1 : 0,
+                            reinterpret_cast<int32_t*>(ws + L.block_off),
                             reinterpret_cast<int32_t*>(ws + L.plan),
                             reinterpret_cast<int32_t*>(ws + L.expert_count),
                             reinterpret_cast<int32_t*>(ws + L.expert_base),
@@ -717,7 +719,8 @@ cudaError_t launch_route_permute(const void* logits, int logits_dtype, const voi
     return cudaGetLastError();
   });
   if (e != cudaSuccess) return e;
-  (void)launch_pdl(k_scan, 1, 1024, 0, s, bf.block_hist, nblocks, E, H, I, num_sms, bf.block_off, bf.plan,
+  (void)launch_pdl(k_scan, 1, 1024, 0, s, bf.block_hist, nblocks, E, H, I, num_sms,
+                   T <= kSplitMaxT ? 1 : 0, bf.block_off, bf.plan,
                             bf.expert_count, bf.expert_base, bf.counters, bf.status);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
