@@ -249,11 +249,11 @@ cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias,
 //                 e4m3 rows and 128-column scales of its picks into the permuted buffers and
 //                 zero-fills the padding slots it owns.
 // ------------------------------------------------------------------------------------------
-// K splits per tile for a persistent grid of G CTAs, used only when there are fewer tiles than
-// CTAs (split units cost a partial-tile round trip and a fence each). Cost, in K blocks on the
-// busiest CTA: waves * ceil(nkb / s) plus per-unit overheads. Ties keep the smaller split.
+// K splits per tile for a persistent grid of G CTAs, allowed for small batches only (a split
+// unit stores its partial tile and k_split_finish sums them). Cost, in quarter K blocks on the
+// busiest CTA: 4 * waves * ceil(nkb / s) plus per-unit overheads. Ties keep the smaller split.
 __device__ int choose_split(int tiles, int nkb, int G, int allow) {
-  if (!allow || tiles <= 0 || tiles >= G) return 1;
+  if (!allow || tiles <= 0) return 1;
   int best = 1;
   long best_cost = 0x7fffffffffffL;
   for (int s = 1; s <= kMaxSplit && s <= nkb; ++s) {
