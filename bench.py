@@ -30,13 +30,18 @@ sys.path.insert(0, ROOT)
 from flashinfer_b200 import _lib, moe as fmoe, workload as wl  # noqa: E402
 
 METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
-SMALL_T = 32           # T <= SMALL_T: fused route/plan/scatter kernel, split-K finish kernels
+SMALL_T = 64           # T <= SMALL_T: fused route/plan/scatter cluster kernel
+SPLIT_MAX_T = 32       # T <= SPLIT_MAX_T: split-K finish kernel after each GEMM
 
 
 def kernels_per_call(T: int) -> int:
     """Launches of one call: route+hist, scan, scatter, gather, gemm1, gemm2, combine; for
-    T <= SMALL_T the fused plan kernel replaces the first three and a split-K finish kernel
-    follows each GEMM."""
+    T <= SMALL_T the fused plan kernel replaces the first three, and for T <= SPLIT_MAX_T a
+    split-K finish kernel follows each GEMM."""
+    if T <= SPLIT_MAX_T:
+        return 7
+    if T <= SMALL_T:
+        return 5
     return 7
 
 

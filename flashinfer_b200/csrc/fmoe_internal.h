@@ -132,8 +132,10 @@ cudaError_t launch_gather(const RunParams& p, cudaStream_t s);
 // SMs; the split partial tiles are finished by launch_split_finish(kind) after each GEMM.
 constexpr int kSplitMaxT = 32;
 cudaError_t launch_split_finish(const RunParams& p, int kind, cudaStream_t s);
-// T <= kSmallT: routing + histogram + plan + scatter in one CTA (replaces the three above)
-constexpr int kSmallT = 32;
+// T <= kSmallT: routing + histogram + plan + scatter in one kernel (replaces the three above):
+// one CTA per 32 tokens, the CTAs of a cluster exchange counts through distributed shared memory
+constexpr int kSmallTokensPerCta = 32;
+constexpr int kSmallT = 2 * kSmallTokensPerCta;
 cudaError_t launch_plan_small(const RunParams& p, cudaStream_t s);
 cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUtensorMap& tm_w1,
                          const CUtensorMap& tm_sa, cudaStream_t s);
@@ -203,6 +205,27 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+// The same with a thread-block cluster of cluster_x CTAs along x (grid.x a multiple of it).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block,
+                                      size_t smem, cudaStream_t s, int cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 

@@ -12,6 +12,7 @@
 #include <math.h>
 
 #include "fmoe_internal.h"
+#include "fmoe_ptx.cuh"
 
 namespace fmoe {
 
@@ -280,6 +281,7 @@ __device__ void write_plan(const int* cnt, int E, int H, int I, int G, int allow
     pairs += cnt[e];
   }
   base[E] = acc;
+  if (plan == nullptr) return;
   const int mtiles = acc / kTileM;
   const int tiles1 = mtiles * (I / kBlock);
   const int tiles2 = mtiles * (H / kTileN);
@@ -459,43 +461,56 @@ __global__ void __launch_bounds__(256) k_scatter(
   }
 }
 
-// Small batches (T <= kSmallT): routing, the histogram, the plan and the scatter in one CTA,
-// replacing k_route_hist + k_scan + k_scatter (three dependent launches of a few tokens each).
-// Same results: the plan comes from write_plan, a token's slot rank for expert e is the number
-// of earlier tokens that picked e (stable, tokens ascending; a popcount of the expert's token
-// mask), its picks are listed by ascending
-// expert, and padding slots are marked empty.
+// Small batches (T <= kSmallT): routing, the histogram, the plan and the scatter in one
+// kernel, replacing k_route_hist + k_scan + k_scatter (three dependent launches of a few tokens
+// each). One cluster of ceil(T / 32) CTAs; CTA r routes tokens [32r, 32r + 32), one token per
+// warp, and keeps per local expert its token count and a mask of its tokens that picked the
+// expert. After one cluster barrier every CTA reads the other CTAs' counts through distributed
+// shared memory: the totals give the plan and the expert bases (the same serial scan in every
+// CTA), the counts of lower-ranked CTAs give the rank offset of this CTA's tokens. Same results
+// as the three-kernel path: a token's slot rank for expert e is the number of earlier tokens that
+// picked e (stable, tokens ascending), its picks are listed by ascending expert, and padding
+// slots are marked empty.
 template <typename TL, typename TB>
 __global__ void __launch_bounds__(1024) k_plan_small(
     const TL* __restrict__ logits, const TB* __restrict__ bias, int T, float rsf, int local_start,
-    int E, int H, int I, int G, int32_t* __restrict__ ids_out, float* __restrict__ w_out,
-    int32_t* __restrict__ plan, int32_t* __restrict__ expert_count,
+    int E, int H, int I, int G, int allow_split, int32_t* __restrict__ ids_out,
+    float* __restrict__ w_out, int32_t* __restrict__ plan, int32_t* __restrict__ expert_count,
     int32_t* __restrict__ expert_base, int32_t* __restrict__ counters,
     int32_t* __restrict__ status, int32_t* __restrict__ slot_token,
     float* __restrict__ slot_weight, int32_t* __restrict__ token_slot,
     float* __restrict__ token_weight) {
-  __shared__ int cnt[kMaxLocalExperts];
+  constexpr int kTok = kSmallTokensPerCta;
+  __shared__ int cnt[kMaxLocalExperts];       // this CTA's tokens per local expert
+  __shared__ int tot[kMaxLocalExperts];       // all tokens per local expert
+  __shared__ int off[kMaxLocalExperts];       // tokens of lower-ranked CTAs per local expert
   __shared__ int base[kMaxLocalExperts + 1];
-  __shared__ int ids_s[kSmallT][kTopK];
-  __shared__ uint32_t tokmask[kMaxLocalExperts][kSmallT / 32];  // tokens that picked expert e
+  __shared__ uint32_t tokmask[kMaxLocalExperts];  // bit i: token 32r + i picked the expert
+  __shared__ int ids_s[kTok][kTopK];
+  __shared__ float w_s[kTok][kTopK];
   pdl_begin();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+  const uint32_t rank = cluster_ctarank(), ncta = cluster_nctarank();
+  const int t0 = static_cast<int>(rank) * kTok;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     cnt[e] = 0;
-#pragma unroll
-    for (int wd = 0; wd < kSmallT / 32; ++wd) tokmask[e][wd] = 0u;
+    tokmask[e] = 0u;
   }
   __syncthreads();
-  float b[8];
-  load8<TB>(bias + lane * 8, b);
-  for (int t = warp; t < T; t += nwarp) {
+  if (warp < kTok && t0 + warp < T) {
+    const int t = t0 + warp;
+    float b[8];
+    load8<TB>(bias + lane * 8, b);
     int ids[kTopK];
     float w[kTopK];
     route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, lane, ids, w);
     if (lane == 0) {
       store_picks(ids_out, w_out, t, ids, w);
 #pragma unroll
-      for (int k = 0; k < kTopK; ++k) ids_s[t][k] = ids[k];
+      for (int k = 0; k < kTopK; ++k) {
+        ids_s[warp][k] = ids[k];
+        w_s[warp][k] = w[k];
+      }
     }
     if (lane < kTopK) {
       int mine = ids[0];
@@ -505,23 +520,38 @@ __global__ void __launch_bounds__(1024) k_plan_small(
       const int le = mine - local_start;
       if (le >= 0 && le < E) {
         atomicAdd(&cnt[le], 1);
-        atomicOr(&tokmask[le][t >> 5], 1u << (t & 31));
+        atomicOr(&tokmask[le], 1u << warp);
       }
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) write_plan(cnt, E, H, I, G, 1, base, plan, status);
-  // token t (thread t): its local picks in ascending expert order
-  const int t = threadIdx.x;
+  cluster_arrive();  // counts of every CTA are complete and visible cluster-wide
+  cluster_wait();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int sum = 0, lower = 0;
+    for (uint32_t r = 0; r < ncta; ++r) {
+      const int c = r == rank ? cnt[e] : ld_dsmem_s32(&cnt[e], r);
+      sum += c;
+      if (r < rank) lower += c;
+    }
+    tot[e] = sum;
+    off[e] = lower;
+  }
+  cluster_arrive();  // this CTA's remote reads are done; matched by the wait before exit
+  __syncthreads();
+  if (threadIdx.x == 0)
+    write_plan(tot, E, H, I, G, allow_split, base, rank == 0 ? plan : nullptr, status);
+  // token t0 + i (thread i < 32): its local picks in ascending expert order
+  const int i = threadIdx.x;
+  const int t = t0 + i;
   int le[kTopK];
   float lw[kTopK];
   int nloc = 0;
-  if (t < T) {
+  if (i < kTok && t < T) {
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
-      const int e = ids_s[t][k] - local_start;
+      const int e = ids_s[i][k] - local_start;
       if (e >= 0 && e < E) {
-        const float w = w_out[static_cast<size_t>(t) * kTopK + k];
         int j = nloc;  // insertion into the ascending list le[0..nloc)
         while (j > 0 && le[j - 1] > e) {
           le[j] = le[j - 1];
@@ -529,33 +559,30 @@ __global__ void __launch_bounds__(1024) k_plan_small(
           --j;
         }
         le[j] = e;
-        lw[j] = w;
+        lw[j] = w_s[i][k];
         ++nloc;
       }
     }
   }
   __syncthreads();  // base[] is visible
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    expert_count[e] = cnt[e];
-    expert_base[e] = base[e];
+  if (rank == 0) {
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      expert_count[e] = tot[e];
+      expert_base[e] = base[e];
+    }
+    if (threadIdx.x == 0) expert_base[E] = base[E];
   }
-  if (threadIdx.x == 0) expert_base[E] = base[E];
-  for (int i = threadIdx.x; i < 2 * kMaxSplitUnits; i += blockDim.x) counters[i] = 0;
-  if (t < T) {
+  for (int c = threadIdx.x + static_cast<int>(rank) * blockDim.x; c < 2 * kMaxSplitUnits;
+       c += ncta * blockDim.x)
+    counters[c] = 0;
+  if (i < kTok && t < T) {
     int* ts = token_slot + static_cast<size_t>(t) * kTopK;
     float* tw = token_weight + static_cast<size_t>(t) * kTopK;
+    const uint32_t below = (1u << i) - 1u;
     for (int j = 0; j < kTopK; ++j) {
       if (j < nloc) {
         const int e = le[j];
-        // rank among the tokens that picked e = earlier tokens in its token mask
-        int rank = 0;
-#pragma unroll
-        for (int wd = 0; wd < kSmallT / 32; ++wd) {
-          const int lo = wd * 32;
-          const uint32_t below = t >= lo + 32 ? 0xffffffffu : (t <= lo ? 0u : (1u << (t - lo)) - 1u);
-          rank += __popc(tokmask[e][wd] & below);
-        }
-        const int slot = base[e] + rank;
+        const int slot = base[e] + off[e] + __popc(tokmask[e] & below);
         slot_token[slot] = t;
         slot_weight[slot] = lw[j];
         ts[j] = slot;
@@ -566,11 +593,14 @@ __global__ void __launch_bounds__(1024) k_plan_small(
       }
     }
   }
-  for (int e = warp; e < E; e += nwarp)
-    for (int sl = base[e] + cnt[e] + lane; sl < base[e + 1]; sl += 32) {
+  // padding slots: expert e by warp (e / ncta) of CTA e mod ncta
+  for (int e = warp * static_cast<int>(ncta) + static_cast<int>(rank); e < E;
+       e += nwarp * static_cast<int>(ncta))
+    for (int sl = base[e] + tot[e] + lane; sl < base[e + 1]; sl += 32) {
       slot_token[sl] = -1;
       slot_weight[sl] = 0.0f;
     }
+  cluster_wait();  // no CTA exits while another may still read its counts
 }
 
 // Gather: one warp per token reads the token's e4m3 row once (7168 B = 14 x 16 B per lane)
@@ -681,14 +711,23 @@ cudaError_t launch_gather(const RunParams& p, cudaStream_t s) {
 
 cudaError_t launch_plan_small(const RunParams& p, cudaStream_t s) {
   if (p.T <= 0) return cudaSuccess;
+  if (p.T > kSmallT) return cudaErrorInvalidValue;
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
   return dispatch_dtypes(p.logits_dtype, p.bias_dtype, [&](auto tl, auto tb) {
     using TL = decltype(tl);
     using TB = decltype(tb);
-    (void)launch_pdl(k_plan_small<TL, TB>, 1, 1024, 0, s, static_cast<const TL*>(p.logits),
+    // one CTA runs as the implicit single-CTA cluster (no cluster launch attribute)
+    const int ncta = (p.T + kSmallTokensPerCta - 1) / kSmallTokensPerCta;
+    auto kern = k_plan_small<TL, TB>;
+    auto launch = [&](auto... a) {
+      return ncta == 1 ? launch_pdl(kern, 1, 1024, 0, s, a...)
+                       : launch_pdl_cluster(kern, ncta, 1024, 0, s, ncta, a...);
+    };
+    (void)launch(static_cast<const TL*>(p.logits),
                      static_cast<const TB*>(p.bias), p.T, p.rsf, p.local_start, p.E, p.H, p.I,
-                     p.num_sms, reinterpret_cast<int32_t*>(ws + L.topk_ids),
+                     p.num_sms, p.T <= kSplitMaxT ? 1 : 0,
+                     reinterpret_cast<int32_t*>(ws + L.topk_ids),
                      reinterpret_cast<float*>(ws + L.topk_w), reinterpret_cast<int32_t*>(ws + L.plan),
                      reinterpret_cast<int32_t*>(ws + L.expert_count),
                      reinterpret_cast<int32_t*>(ws + L.expert_base),
