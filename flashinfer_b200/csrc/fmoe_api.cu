@@ -263,8 +263,8 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   CUtensorMap tm_a, tm_w1, tm_hi, tm_lo, tm_w2, tm_sa1, tm_sa2;
   if (!make_tmap_u8(&tm_a, p.ws + L.a_perm, H, L.cap, H, 128, 128) ||
       !make_tmap_u8(&tm_w1, a->gemm1_weights, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128) ||
-      !make_tmap_u8(&tm_hi, p.ws + L.h_hi, I, L.cap, I, 128, 128) ||
-      !make_tmap_u8(&tm_lo, p.ws + L.h_lo, I, L.cap, I, 128, 128) ||
+      !make_tmap_u8(&tm_hi, p.ws + L.h_hi, I, L.cap, I, 128, T <= kPackedMaxT ? 64 : 128) ||
+      !make_tmap_u8(&tm_lo, p.ws + L.h_lo, I, L.cap, I, 128, T <= kPackedMaxT ? 64 : 128) ||
       !make_tmap_u8(&tm_w2, a->gemm2_weights, I, static_cast<uint64_t>(E) * H, I, 128, 256) ||
       // per-K-block activation scales, [K blocks][cap] fp32: one 128-slot row per load
       !make_tmap_f32_rows(&tm_sa1, p.ws + L.a_scale_t, L.cap, H / kBlock, 128) ||

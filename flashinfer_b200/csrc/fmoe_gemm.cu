@@ -64,6 +64,16 @@ struct Cfg<2> {
   static constexpr int A_TILES = 2;
   static constexpr int STAGE = 128 * 128 * A_TILES + 256 * 128;  // 64 KB
 };
+// GEMM2 for tiles of at most 64 routed slots (T <= kPackedMaxT): one A tile holds the hi term of
+// the tile's first 64 slots in rows 0-63 and their lo term in rows 64-127, so a K block takes
+// four MMAs instead of eight; at the tile end the lo rows' fp32 sums are added to the hi rows'
+// through shared memory (xbuf).
+template <>
+struct Cfg<3> {
+  static constexpr int NS = 3;
+  static constexpr int A_TILES = 1;
+  static constexpr int STAGE = 128 * 128 * A_TILES + 256 * 128;  // 48 KB
+};
 
 constexpr int kThreads = 352;
 constexpr int kEpiWarps = 8;
@@ -76,8 +86,12 @@ constexpr int kATileBytes = 128 * 128;
 constexpr int kSaRing = 8;
 constexpr int kSaBytes = 128 * 4;
 constexpr int kMaxKb = 64;  // K blocks per GEMM (H/128 and I/128); checked on the host
+// KIND 3 lo -> hi exchange: 64 rows of 256 fp32 in accumulator order, rows padded by 4 floats
+// (a warp's 16-byte accesses to consecutive rows then cover all 32 banks)
+constexpr int kXRow = 2 * 128 + 4;
+constexpr int kXBufBytes = 64 * kXRow * 4;
 
-struct GemmTail {
+struct alignas(16) GemmTail {
   uint64_t full[4];
   uint64_t empty[4];
   uint64_t tfull[2];
@@ -97,9 +111,11 @@ struct GemmTail {
 template <int KIND>
 constexpr size_t gemm_smem_bytes() {
   static_assert(Cfg<KIND>::NS + 3 <= kSaRing, "activation-scale ring too short");
+  static_assert(sizeof(GemmTail) % 16 == 0, "xbuf follows the tail 16-byte aligned");
   return static_cast<size_t>(Cfg<KIND>::NS) * Cfg<KIND>::STAGE + kSaRing * kSaBytes +
-         sizeof(GemmTail) + 1024;
+         sizeof(GemmTail) + (KIND == 3 ? kXBufBytes : 0) + 1024;
 }
+static_assert(gemm_smem_bytes<3>() <= 227 * 1024, "KIND 3 shared memory");
 
 struct Unit {
   int e, n, row0, nrows, kb0, kb1;
@@ -264,6 +280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   float* sa_ring = reinterpret_cast<float*>(smem + NS * STAGE);  // [kSaRing][128]
   GemmTail* tail = reinterpret_cast<GemmTail*>(smem + NS * STAGE + kSaRing * kSaBytes);
+  float* xbuf = reinterpret_cast<float*>(tail + 1);  // [64][kXRow], KIND 3 only
   volatile int* abort_flag = &tail->abort_flag;
 
   const int warp = threadIdx.x >> 5;
@@ -289,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tail->abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_a0);
-    if (KIND == 2) tma_prefetch_desc(&tm_a1);
+    if (KIND != 1) tma_prefetch_desc(&tm_a1);
     tma_prefetch_desc(&tm_w);
     tma_prefetch_desc(&tm_sa);
   }
@@ -336,11 +353,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d(st, &tm_a0, &tail->full[s], kx, u.row0, pol_a);
             tma_load_2d(st + kATileBytes, &tm_w, &tail->full[s], kx, wrow, pol_w);
             tma_load_2d(st + 2 * kATileBytes, &tm_w, &tail->full[s], kx, wrow + args.I, pol_w);
-          } else {
+          } else if (KIND == 2) {
             const int wrow = u.e * args.H + u.n * kTileN;
             tma_load_2d(st, &tm_a0, &tail->full[s], kx, u.row0, pol_a);
             tma_load_2d(st + kATileBytes, &tm_a1, &tail->full[s], kx, u.row0, pol_a);
             tma_load_2d(st + 2 * kATileBytes, &tm_w, &tail->full[s], kx, wrow, pol_w);
+          } else {  // 64-row boxes: hi rows 0-63, lo rows 64-127 of the one A tile
+            const int wrow = u.e * args.H + u.n * kTileN;
+            tma_load_2d(st, &tm_a0, &tail->full[s], kx, u.row0, pol_a);
+            tma_load_2d(st + kATileBytes / 2, &tm_a1, &tail->full[s], kx, u.row0, pol_a);
+            tma_load_2d(st + kATileBytes, &tm_w, &tail->full[s], kx, wrow, pol_w);
           }
           last_round[s] = r;
         }
@@ -403,7 +425,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = warp - 2;
     const int g = ew >> 2;        // column group: 0 -> cols [0,64)+[128,192), 1 -> [64,128)+...
     const int q = warp & 3;       // TMEM lane quarter this warp may access
-    const int r = q * 32 + lane;  // tile row (slot) owned by this thread
+    const int r = q * 32 + lane;  // accumulator row owned by this thread
+    // Slot offset of that row within the tile, and (KIND 3) whether it holds the lo term.
+    const int prow = KIND == 3 ? (r & 63) : r;
+    const bool lo_row = KIND == 3 && r >= 64;
     const int etid = ew * 32 + lane;
     const int64_t cap = args.cap;
     int kt = 0;
@@ -437,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(1, kEpiWarps * 32);
       // Warps whose 32 rows are all padding skip the TMEM reads (their rows are discarded);
       // they still wait for each half before releasing it, which keeps the phases aligned.
-      const bool warp_rows = q * 32 < u.nrows;
+      const bool warp_rows = (KIND == 3 ? (q & 1) : q) * 32 < u.nrows;
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
       const bool has_next = unit + static_cast<int>(gridDim.x) < units;
@@ -463,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_32x32b_x16(taddr + g * 64, va);
           // the activation scale reached shared memory before the MMA that this wait follows;
           // the shared-memory reads overlap the first TMEM load
-          const float sa = sa_ring[(kt % kSaRing) * 128 + r];
+          const float sa = sa_ring[(kt % kSaRing) * 128 + prow];
           const float f0 = sa * tail->w_sc[par][0][kb];
           const float f1 = sa * tail->w_sc[par][1][kb];
           tmem_ld_wait16(va);
@@ -490,16 +515,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       // w_sc[par ^ 1] was last read in the previous unit, which every epilogue thread has left
       if (has_next) store_w_scale(par ^ 1, w_next);
 
-      const bool valid = r < u.nrows;
-      const size_t row = static_cast<size_t>(u.row0) + r;
+      if (KIND == 3) {
+        // add the lo rows' sums to the hi rows' (same slot, same columns, same scales)
+        const bool routed = prow < u.nrows;
+        float4* x = reinterpret_cast<float4*>(xbuf + prow * kXRow + g * 128);
+        if (lo_row && routed) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            x[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+        }
+        named_bar_sync(1, kEpiWarps * 32);
+        if (!lo_row && routed) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float4 v = x[i];
+            acc[4 * i] += v.x;
+            acc[4 * i + 1] += v.y;
+            acc[4 * i + 2] += v.z;
+            acc[4 * i + 3] += v.w;
+          }
+        }
+      }
+      const bool valid = prow < u.nrows && !lo_row;
+      const size_t row = static_cast<size_t>(u.row0) + prow;
       if (S > 1) {
         // split-K: publish this split's partial tile (valid rows); k_split_finish sums the
         // splits of each tile in split order and runs the epilogue
         if (valid) {
-          float* p = args.partials + (static_cast<size_t>(unit) * args.partial_rows + r) * kTileN;
+          float* pr = args.partials + (static_cast<size_t>(unit) * args.partial_rows + prow) * kTileN;
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            float4* dst = reinterpret_cast<float4*>(p + h * 128 + g * 64);
+            float4* dst = reinterpret_cast<float4*>(pr + h * 128 + g * 64);
 #pragma unroll
             for (int i = 0; i < 16; ++i)
               dst[i] = make_float4(acc[h * 64 + 4 * i], acc[h * 64 + 4 * i + 1],
@@ -731,6 +777,7 @@ cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUte
 
 cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
                          const CUtensorMap& tm_w2, const CUtensorMap& tm_sa, cudaStream_t s) {
+  if (p.T <= kPackedMaxT) return launch_gemm_kind<3>(p, tm_hi, tm_lo, tm_w2, tm_sa, s);
   return launch_gemm_kind<2>(p, tm_hi, tm_lo, tm_w2, tm_sa, s);
 }
 

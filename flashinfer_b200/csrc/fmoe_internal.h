@@ -137,6 +137,9 @@ cudaError_t launch_split_finish(const RunParams& p, int kind, cudaStream_t s);
 constexpr int kSmallTokensPerCta = 32;
 constexpr int kSmallT = 2 * kSmallTokensPerCta;
 cudaError_t launch_plan_small(const RunParams& p, cudaStream_t s);
+// GEMM2 for T <= kPackedMaxT (every tile then has at most 64 routed slots) packs the hi and lo
+// terms of a tile's first 64 slots into one A tile; tm_hi and tm_lo then have 64-row boxes.
+constexpr int kPackedMaxT = 64;
 cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUtensorMap& tm_w1,
                          const CUtensorMap& tm_sa, cudaStream_t s);
 cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
