@@ -269,7 +269,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(NS >= 2 && NS <= 4, "barrier arrays hold 4 stages; alternating producers need 2");
   constexpr int STAGE = C::STAGE;
   constexpr int kErr = KIND == 1 ? FMOE_STATUS_TIMEOUT_GEMM1 : FMOE_STATUS_TIMEOUT_GEMM2;
-  pdl_begin();
+  // Until griddepcontrol.wait below, the previous kernel may still run: its predecessor-ordered
+  // launch (pdl_begin_in_order) guarantees only that the plan and the expert tables are complete.
+  // The prologue and the weight loads of the first NS K iterations, which need nothing else,
+  // run before the wait; the activations are loaded after it.
 
   const int S = args.plan[KIND == 1 ? kPlanSplit1 : kPlanSplit2];
   const int units = args.plan[KIND == 1 ? kPlanUnits1 : kPlanUnits2];
@@ -319,6 +322,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tail->tmem_base;
 
+  // The weight boxes of iteration it (K block kb of unit u) into stage s, with the stage's
+  // transaction count for the whole stage (weights, activations and activation scales).
+  auto issue_weights = [&](int s, const Unit& u, int kb, uint64_t pol_w) {
+    uint8_t* st = smem + s * STAGE;
+    mbar_arrive_expect_tx(&tail->full[s], STAGE + kSaBytes);
+    const int kx = kb * kBlock;
+    if (KIND == 1) {
+      const int wrow = u.e * 2 * args.I + u.n * kBlock;
+      tma_load_2d(st + kATileBytes, &tm_w, &tail->full[s], kx, wrow, pol_w);
+      tma_load_2d(st + 2 * kATileBytes, &tm_w, &tail->full[s], kx, wrow + args.I, pol_w);
+    } else {
+      tma_load_2d(st + C::A_TILES * kATileBytes, &tm_w, &tail->full[s], kx,
+                  u.e * args.H + u.n * kTileN, pol_w);
+    }
+  };
+  if ((warp == 0 || warp == kProducer2Warp) && lane == 0) {
+    const int pw = warp == 0 ? 0 : 1;
+    const uint64_t pol_w = policy_evict_first();
+    int it = 0;
+    for (int unit = blockIdx.x; unit < units && it < NS; unit += gridDim.x) {
+      const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
+      for (int kb = u.kb0; kb < u.kb1 && it < NS; ++kb, ++it)
+        if ((it & 1) == pw) issue_weights(it, u, kb, pol_w);
+    }
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+
   if (warp == 0 || warp == kProducer2Warp) {
     // ------------------------------------------------------------------ TMA producers
     const int pw = warp == 0 ? 0 : 1;  // issues the K iterations it with (it & 1) == pw
@@ -345,24 +376,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* st = smem + s * STAGE;
-          mbar_arrive_expect_tx(&tail->full[s], STAGE + kSaBytes);
+          if (it >= NS) issue_weights(s, u, kb, pol_w);  // else issued before the wait
           const int kx = kb * kBlock;
           tma_load_2d(sa_ring + (it % kSaRing) * 128, &tm_sa, &tail->full[s], u.row0, kb, pol_a);
           if (KIND == 1) {
-            const int wrow = u.e * 2 * args.I + u.n * kBlock;
             tma_load_2d(st, &tm_a0, &tail->full[s], kx, u.row0, pol_a);
-            tma_load_2d(st + kATileBytes, &tm_w, &tail->full[s], kx, wrow, pol_w);
-            tma_load_2d(st + 2 * kATileBytes, &tm_w, &tail->full[s], kx, wrow + args.I, pol_w);
           } else if (KIND == 2) {
-            const int wrow = u.e * args.H + u.n * kTileN;
             tma_load_2d(st, &tm_a0, &tail->full[s], kx, u.row0, pol_a);
             tma_load_2d(st + kATileBytes, &tm_a1, &tail->full[s], kx, u.row0, pol_a);
-            tma_load_2d(st + 2 * kATileBytes, &tm_w, &tail->full[s], kx, wrow, pol_w);
           } else {  // 64-row boxes: hi rows 0-63, lo rows 64-127 of the one A tile
-            const int wrow = u.e * args.H + u.n * kTileN;
             tma_load_2d(st, &tm_a0, &tail->full[s], kx, u.row0, pol_a);
             tma_load_2d(st + kATileBytes / 2, &tm_a1, &tail->full[s], kx, u.row0, pol_a);
-            tma_load_2d(st + kATileBytes, &tm_w, &tail->full[s], kx, wrow, pol_w);
           }
           last_round[s] = r;
         }
@@ -615,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // arithmetic as k_gemm's register epilogue.
 template <int KIND>
 __global__ void __launch_bounds__(256) k_split_finish(const GemmArgs args) {
-  pdl_begin();
+  pdl_begin_in_order();  // GEMM2, which follows, reads the plan before its own wait
   const int S = args.plan[KIND == 1 ? kPlanSplit1 : kPlanSplit2];
   if (S <= 1) return;
   const int tiles = args.plan[KIND == 1 ? kPlanTiles1 : kPlanTiles2];

@@ -195,6 +195,14 @@ __device__ __forceinline__ void pdl_begin() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// The same with the order reversed, for a kernel that a GEMM follows: the GEMM reads the work
+// plan before its own wait, and when it starts, its predecessor has passed this wait, so every
+// earlier kernel of the call (the plan kernel included) has completed.
+__device__ __forceinline__ void pdl_begin_in_order() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
                               cudaStream_t s, Args... args) {

@@ -612,7 +612,7 @@ __global__ void __launch_bounds__(256) k_gather_tokens(const int32_t* __restrict
                                                        uint8_t* __restrict__ a_perm,
                                                        float* __restrict__ a_scale_t) {
   constexpr int kMaxVec = 16;  // H <= 8192 (at most 64 scale blocks; 16 B per lane per step)
-  pdl_begin();
+  pdl_begin_in_order();  // GEMM1, which follows, reads the plan before its own wait
   const int lane = threadIdx.x & 31;
   const int warp0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int nwarps = gridDim.x * (blockDim.x >> 5);
