@@ -133,9 +133,10 @@ cudaError_t launch_gather(const RunParams& p, cudaStream_t s);
 constexpr int kSplitMaxT = 32;
 cudaError_t launch_split_finish(const RunParams& p, int kind, cudaStream_t s);
 // T <= kSmallT: routing + histogram + plan + scatter in one kernel (replaces the three above):
-// one CTA per 32 tokens, the CTAs of a cluster exchange counts through distributed shared memory
-constexpr int kSmallTokensPerCta = 32;
-constexpr int kSmallT = 2 * kSmallTokensPerCta;
+// one CTA (one warp per token) per 8 tokens, up to 8 CTAs in one cluster exchanging counts
+// through distributed shared memory
+constexpr int kSmallTokensPerCta = 8;
+constexpr int kSmallT = 8 * kSmallTokensPerCta;
 cudaError_t launch_plan_small(const RunParams& p, cudaStream_t s);
 // GEMM2 for T <= kPackedMaxT (every tile then has at most 64 routed slots) packs the hi and lo
 // terms of a tile's first 64 slots into one A tile; tm_hi and tm_lo then have 64-row boxes.

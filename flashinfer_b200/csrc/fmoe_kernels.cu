@@ -250,53 +250,77 @@ cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias,
 //                 e4m3 rows and 128-column scales of its picks into the permuted buffers and
 //                 zero-fills the padding slots it owns.
 // ------------------------------------------------------------------------------------------
-// K splits per tile for a persistent grid of G CTAs, allowed for small batches only (a split
+// The expert bases padded to 128 slots and the GEMM work plan from the per-expert counts, by one
+// warp (lane l takes experts [8l, 8l+8), a shuffle scan gives the bases); also clears the status
+// word before any GEMM can set it. With plan == nullptr only the bases are written.
+// K splits per tile for a persistent grid of G CTAs are allowed for small batches only (a split
 // unit stores its partial tile and k_split_finish sums them). Cost, in quarter K blocks on the
-// busiest CTA: 4 * waves * ceil(nkb / s) plus per-unit overheads. Ties keep the smaller split.
-__device__ int choose_split(int tiles, int nkb, int G, int allow) {
-  if (!allow || tiles <= 0) return 1;
-  int best = 1;
-  long best_cost = 0x7fffffffffffL;
-  for (int s = 1; s <= kMaxSplit && s <= nkb; ++s) {
-    if (s > 1 && static_cast<long>(tiles) * s > kMaxSplitUnits) break;
-    const long waves = (static_cast<long>(tiles) * s + G - 1) / G;
-    const long per = (nkb + s - 1) / s;
-    const long cost = 4 * waves * per + waves * (s > 1 ? 12 : 8);
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = s;
-    }
+// busiest CTA: 4 * waves * ceil(nkb / s) plus per-unit overheads; the least cost wins, ties to
+// the smaller split. Lanes 0-7 price s = 1..8 for GEMM1, lanes 8-15 for GEMM2.
+__device__ void write_plan_warp(const int* cnt, int E, int H, int I, int G, int allow_split,
+                                int* base, int32_t* plan, int32_t* status, int lane) {
+  constexpr int kPer = kMaxLocalExperts / 32;
+  const int e0 = lane * kPer;
+  int c[kPer];
+  int padded = 0, pairs = 0;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    c[j] = e0 + j < E ? cnt[e0 + j] : 0;
+    padded += (c[j] + kTileM - 1) / kTileM * kTileM;
+    pairs += c[j];
   }
-  return best;
-}
-
-// Expert bases padded to 128 slots and the GEMM work plan from the per-expert counts (one
-// thread); also clears the status word before any GEMM can set it.
-__device__ void write_plan(const int* cnt, int E, int H, int I, int G, int allow_split, int* base,
-                           int32_t* plan, int32_t* status) {
-  int acc = 0, pairs = 0;
-  for (int e = 0; e < E; ++e) {
-    base[e] = acc;
-    acc += (cnt[e] + kTileM - 1) / kTileM * kTileM;
-    pairs += cnt[e];
+  int inc = padded;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, inc, off);
+    if (lane >= off) inc += o;
   }
-  base[E] = acc;
+  int acc = inc - padded;
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    if (e0 + j < E) base[e0 + j] = acc;
+    acc += (c[j] + kTileM - 1) / kTileM * kTileM;
+  }
+  const int total = __shfl_sync(0xffffffffu, inc, 31);
+  if (lane == 0) base[E] = total;
+  pairs = __reduce_add_sync(0xffffffffu, pairs);
   if (plan == nullptr) return;
-  const int mtiles = acc / kTileM;
+  const int mtiles = total / kTileM;
   const int tiles1 = mtiles * (I / kBlock);
   const int tiles2 = mtiles * (H / kTileN);
-  const int s1 = choose_split(tiles1, H / kBlock, G, allow_split);
-  const int s2 = choose_split(tiles2, I / kBlock, G, allow_split);
-  plan[kPlanPairs] = pairs;
-  plan[kPlanPadded] = acc;
-  plan[kPlanMTiles] = mtiles;
-  plan[kPlanSplit1] = s1;
-  plan[kPlanUnits1] = tiles1 * s1;
-  plan[kPlanSplit2] = s2;
-  plan[kPlanUnits2] = tiles2 * s2;
-  plan[kPlanTiles1] = tiles1;
-  plan[kPlanTiles2] = tiles2;
-  status[0] = 0;
+  const int which = lane >> 3;  // 0: GEMM1, 1: GEMM2
+  const int sp = (lane & 7) + 1;
+  const int tiles = which == 0 ? tiles1 : tiles2;
+  const int nkb = which == 0 ? H / kBlock : I / kBlock;
+  long long cost = 0x7fffffffffffffLL;
+  const bool valid = which < 2 && sp <= kMaxSplit &&
+                     (sp == 1 || (allow_split && tiles > 0 && sp <= nkb &&
+                                  static_cast<long long>(tiles) * sp <= kMaxSplitUnits));
+  if (valid) {
+    const long long waves = (static_cast<long long>(tiles) * sp + G - 1) / G;
+    const long long per = (nkb + sp - 1) / sp;
+    cost = 4 * waves * per + waves * (sp > 1 ? 12 : 8);
+  }
+  long long key = cost * 8 + (sp - 1);
+#pragma unroll
+  for (int off = 4; off > 0; off >>= 1) {
+    const long long o = __shfl_xor_sync(0xffffffffu, key, off);
+    key = o < key ? o : key;
+  }
+  const int s1 = static_cast<int>(__shfl_sync(0xffffffffu, key, 0) & 7) + 1;
+  const int s2 = static_cast<int>(__shfl_sync(0xffffffffu, key, 8) & 7) + 1;
+  if (lane == 0) {
+    plan[kPlanPairs] = pairs;
+    plan[kPlanPadded] = total;
+    plan[kPlanMTiles] = mtiles;
+    plan[kPlanSplit1] = s1;
+    plan[kPlanUnits1] = tiles1 * s1;
+    plan[kPlanSplit2] = s2;
+    plan[kPlanUnits2] = tiles2 * s2;
+    plan[kPlanTiles1] = tiles1;
+    plan[kPlanTiles2] = tiles2;
+    status[0] = 0;
+  }
 }
 
 __global__ void __launch_bounds__(1024) k_scan(const int32_t* __restrict__ block_hist,
@@ -348,7 +372,7 @@ __global__ void __launch_bounds__(1024) k_scan(const int32_t* __restrict__ block
     if (lane == 0) cnt[e] = run;
   }
   __syncthreads();
-  if (threadIdx.x == 0) write_plan(cnt, E, H, I, G, allow_split, base, plan, status);
+  if (warp == 0) write_plan_warp(cnt, E, H, I, G, allow_split, base, plan, status, lane);
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     expert_count[e] = cnt[e];
@@ -463,16 +487,16 @@ __global__ void __launch_bounds__(256) k_scatter(
 
 // Small batches (T <= kSmallT): routing, the histogram, the plan and the scatter in one
 // kernel, replacing k_route_hist + k_scan + k_scatter (three dependent launches of a few tokens
-// each). One cluster of ceil(T / 32) CTAs; CTA r routes tokens [32r, 32r + 32), one token per
-// warp, and keeps per local expert its token count and a mask of its tokens that picked the
-// expert. After one cluster barrier every CTA reads the other CTAs' counts through distributed
+// each). One cluster of ceil(T / 8) CTAs of 8 warps; CTA r routes tokens [8r, 8r + 8), one token
+// per warp (the routing's double-precision exponentials are spread over up to 8 SMs), and keeps
+// per local expert its token count and a mask of its tokens that picked the expert. After one cluster barrier every CTA reads the other CTAs' counts through distributed
 // shared memory: the totals give the plan and the expert bases (the same serial scan in every
 // CTA), the counts of lower-ranked CTAs give the rank offset of this CTA's tokens. Same results
 // as the three-kernel path: a token's slot rank for expert e is the number of earlier tokens that
 // picked e (stable, tokens ascending), its picks are listed by ascending expert, and padding
 // slots are marked empty.
 template <typename TL, typename TB>
-__global__ void __launch_bounds__(1024) k_plan_small(
+__global__ void __launch_bounds__(32 * kSmallTokensPerCta) k_plan_small(
     const TL* __restrict__ logits, const TB* __restrict__ bias, int T, float rsf, int local_start,
     int E, int H, int I, int G, int allow_split, int32_t* __restrict__ ids_out,
     float* __restrict__ w_out, int32_t* __restrict__ plan, int32_t* __restrict__ expert_count,
@@ -485,7 +509,7 @@ __global__ void __launch_bounds__(1024) k_plan_small(
   __shared__ int tot[kMaxLocalExperts];       // all tokens per local expert
   __shared__ int off[kMaxLocalExperts];       // tokens of lower-ranked CTAs per local expert
   __shared__ int base[kMaxLocalExperts + 1];
-  __shared__ uint32_t tokmask[kMaxLocalExperts];  // bit i: token 32r + i picked the expert
+  __shared__ uint32_t tokmask[kMaxLocalExperts];  // bit i: token 8r + i picked the expert
   __shared__ int ids_s[kTok][kTopK];
   __shared__ float w_s[kTok][kTopK];
   pdl_begin();
@@ -539,9 +563,10 @@ __global__ void __launch_bounds__(1024) k_plan_small(
   }
   cluster_arrive();  // this CTA's remote reads are done; matched by the wait before exit
   __syncthreads();
-  if (threadIdx.x == 0)
-    write_plan(tot, E, H, I, G, allow_split, base, rank == 0 ? plan : nullptr, status);
-  // token t0 + i (thread i < 32): its local picks in ascending expert order
+  if (warp == 0)
+    write_plan_warp(tot, E, H, I, G, allow_split, base, rank == 0 ? plan : nullptr, status,
+                    lane);
+  // token t0 + i (thread i < 8): its local picks in ascending expert order
   const int i = threadIdx.x;
   const int t = t0 + i;
   int le[kTopK];
@@ -721,8 +746,8 @@ cudaError_t launch_plan_small(const RunParams& p, cudaStream_t s) {
     const int ncta = (p.T + kSmallTokensPerCta - 1) / kSmallTokensPerCta;
     auto kern = k_plan_small<TL, TB>;
     auto launch = [&](auto... a) {
-      return ncta == 1 ? launch_pdl(kern, 1, 1024, 0, s, a...)
-                       : launch_pdl_cluster(kern, ncta, 1024, 0, s, ncta, a...);
+      return ncta == 1 ? launch_pdl(kern, 1, 32 * kSmallTokensPerCta, 0, s, a...)
+                       : launch_pdl_cluster(kern, ncta, 32 * kSmallTokensPerCta, 0, s, ncta, a...);
     };
     (void)launch(static_cast<const TL*>(p.logits),
                      static_cast<const TB*>(p.bias), p.T, p.rsf, p.local_start, p.E, p.H, p.I,

@@ -75,9 +75,9 @@ def test_routing_bf16_logits_and_fp32_bias():
     np.testing.assert_array_equal(w.cpu().numpy().view(np.uint32), ow.view(np.uint32))
 
 
-@pytest.mark.parametrize("name,local_start", [("t16_s0", 0), ("t256_s5_skew", 0),
-                                              ("t1024_s6", 0), ("t16384_s9", 0),
-                                              ("ep_t16384_s10", 96)])
+@pytest.mark.parametrize("name,local_start", [("t16_s0", 0), ("t32_s3", 0), ("t64_s4", 0),
+                                              ("t256_s5_skew", 0), ("t1024_s6", 0),
+                                              ("t16384_s9", 0), ("ep_t16384_s10", 96)])
 def test_permutation_bit_exact(name, local_start, gpu_weights):
     cfg = ALL[name]
     act = cfg.activations()
@@ -206,6 +206,35 @@ def test_all_tokens_on_one_expert(gpu_weights, cpu_weights):
     assert int(view.expert_count()[5]) == T
     bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
     sel = np.array([0, 1, 127, 128, 255, 256, 299])
+    ref = oracle_rows(act, cfg, sel, cpu_weights)
+    frac, err = omoe.allclose_report(bits[sel], ref, atol=ATOL, rtol=RTOL)
+    assert frac == 1.0, (frac, err)
+
+
+@pytest.mark.parametrize("T", [33, 40, 63, 64])
+def test_small_batch_one_hot_expert(T, gpu_weights, cpu_weights):
+    """Every token picks local expert 7: one tile holds all T slots. Covers the two-CTA routing
+    cluster (T > 32: the second CTA's ranks start after the first CTA's count) and GEMM2's packed
+    hi/lo tile up to its full 64 rows, across the 32-row lane-quarter boundary."""
+    act = wl.make_activations(T, 500 + T)
+    act.routing_logits[:, 7] += 30.0
+    act.routing_bias[7] = 1.0
+    cfg = wl.Config(f"hot7_t{T}", T, 500 + T)
+    out, ws, lay = run_gpu(act, gpu_weights, cfg)
+    view = fmoe.WorkspaceView(ws, lay, T, 32, wl.HIDDEN, wl.INTER)
+    oids, ow = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), cfg.rsf)
+    lid, lw = orouting.local_view(oids, ow, 0, 32)
+    counts, offsets, stoks, sw = orouting.permute(lid, lw, 32)
+    assert counts[7] == T
+    np.testing.assert_array_equal(view.expert_count().cpu().numpy(), counts)
+    base = view.expert_base().cpu().numpy()
+    slot_tok = view.slot_token().cpu().numpy()
+    for e in range(32):
+        np.testing.assert_array_equal(slot_tok[base[e]:base[e] + counts[e]],
+                                      stoks[offsets[e]:offsets[e + 1]])
+        assert np.all(slot_tok[base[e] + counts[e]:base[e + 1]] == -1)
+    bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
+    sel = np.array(sorted({0, 1, 31, 32, T // 2, T - 2, T - 1}))
     ref = oracle_rows(act, cfg, sel, cpu_weights)
     frac, err = omoe.allclose_report(bits[sel], ref, atol=ATOL, rtol=RTOL)
     assert frac == 1.0, (frac, err)
