@@ -86,10 +86,17 @@ constexpr int kATileBytes = 128 * 128;
 constexpr int kSaRing = 8;
 constexpr int kSaBytes = 128 * 4;
 constexpr int kMaxKb = 64;  // K blocks per GEMM (H/128 and I/128); checked on the host
-// KIND 3 lo -> hi exchange: 64 rows of 256 fp32 in accumulator order, rows padded by 4 floats
-// (a warp's 16-byte accesses to consecutive rows then cover all 32 banks)
+// Row buffer of the tile end (xbuf): per tile row the 256 fp32 sums in accumulator order (column
+// group g at g * 128: its 64 first-half columns, then its 64 second-half columns), rows padded
+// by 4 floats (a warp's 16-byte accesses to consecutive rows then cover all 32 banks). It holds
+// the rows of a tile with at most kXSmall routed rows, which all epilogue threads then finish,
+// and for KIND 3 the lo rows of up to 64 slots.
 constexpr int kXRow = 2 * 128 + 4;
-constexpr int kXBufBytes = 64 * kXRow * 4;
+constexpr int kXSmall = 16;
+template <int KIND>
+constexpr int xbuf_bytes() {
+  return (KIND == 3 ? 64 : kXSmall) * kXRow * 4;
+}
 
 struct alignas(16) GemmTail {
   uint64_t full[4];
@@ -113,9 +120,11 @@ constexpr size_t gemm_smem_bytes() {
   static_assert(Cfg<KIND>::NS + 3 <= kSaRing, "activation-scale ring too short");
   static_assert(sizeof(GemmTail) % 16 == 0, "xbuf follows the tail 16-byte aligned");
   return static_cast<size_t>(Cfg<KIND>::NS) * Cfg<KIND>::STAGE + kSaRing * kSaBytes +
-         sizeof(GemmTail) + (KIND == 3 ? kXBufBytes : 0) + 1024;
+         sizeof(GemmTail) + xbuf_bytes<KIND>() + 1024;
 }
-static_assert(gemm_smem_bytes<3>() <= 227 * 1024, "KIND 3 shared memory");
+static_assert(gemm_smem_bytes<1>() <= 227 * 1024 && gemm_smem_bytes<2>() <= 227 * 1024 &&
+                  gemm_smem_bytes<3>() <= 227 * 1024,
+              "shared memory per CTA");
 
 struct Unit {
   int e, n, row0, nrows, kb0, kb1;
@@ -283,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   float* sa_ring = reinterpret_cast<float*>(smem + NS * STAGE);  // [kSaRing][128]
   GemmTail* tail = reinterpret_cast<GemmTail*>(smem + NS * STAGE + kSaRing * kSaBytes);
-  float* xbuf = reinterpret_cast<float*>(tail + 1);  // [64][kXRow], KIND 3 only
+  float* xbuf = reinterpret_cast<float*>(tail + 1);  // [kXSmall or 64][kXRow]
   volatile int* abort_flag = &tail->abort_flag;
 
   const int warp = threadIdx.x >> 5;
@@ -539,6 +548,96 @@ __global__ void __launch_bounds__(kThreads, 1)
       // w_sc[par ^ 1] was last read in the previous unit, which every epilogue thread has left
       if (has_next) store_w_scale(par ^ 1, w_next);
 
+      if (S == 1 && u.nrows <= kXSmall) {
+        // A tile with few routed rows (the decode case): their owners -- the warps of one or
+        // (KIND 3) two lane quarters -- park the rows' fp32 sums in xbuf (KIND 3: lo rows
+        // first, then the hi rows add theirs), and every epilogue thread finishes one row's 8
+        // intermediate columns (KIND 1) or 16 output columns (KIND 2/3): thread etid takes row
+        // etid / 16, column chunk etid % 16, and the row maximum is a 16-lane shuffle
+        // reduction. Each value sees the same operations as on the per-row path below.
+        const bool own = prow < u.nrows;
+        float4* x = reinterpret_cast<float4*>(xbuf + prow * kXRow + g * 128);
+        if (KIND == 3) {
+          if (lo_row && own) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              x[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+          }
+          named_bar_sync(1, kEpiWarps * 32);
+          if (!lo_row && own) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float4 v = x[i];
+              x[i] = make_float4(acc[4 * i] + v.x, acc[4 * i + 1] + v.y, acc[4 * i + 2] + v.z,
+                                 acc[4 * i + 3] + v.w);
+            }
+          }
+        } else if (own) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            x[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
+        }
+        named_bar_sync(1, kEpiWarps * 32);
+        const int rr = etid >> 4, c = etid & 15;
+        const bool live = rr < u.nrows;
+        const float* xr = xbuf + rr * kXRow;
+        const size_t orow = static_cast<size_t>(u.row0) + rr;
+        if (KIND == 1) {
+          // intermediate columns hc + [0, 8): gate (first half) and up (second half) sums
+          const int hc = c * 8;
+          const float* gp = xr + (hc >> 6) * 128 + (hc & 63);
+          float gv[8], uv[8];
+          *reinterpret_cast<float4*>(gv) = *reinterpret_cast<const float4*>(gp);
+          *reinterpret_cast<float4*>(gv + 4) = *reinterpret_cast<const float4*>(gp + 4);
+          *reinterpret_cast<float4*>(uv) = *reinterpret_cast<const float4*>(gp + 64);
+          *reinterpret_cast<float4*>(uv + 4) = *reinterpret_cast<const float4*>(gp + 68);
+          float h[8];
+          float m = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            h[j] = swiglu(uv[j], gv[j]);
+            m = fmaxf(m, fabsf(h[j]));
+          }
+#pragma unroll
+          for (int off = 8; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+          if (live) {
+            const float inv = m > 0.0f ? 448.0f / m : 0.0f;
+            uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+#pragma unroll
+            for (int pr = 0; pr < 4; ++pr) {
+              const float x0 = h[2 * pr] * inv, x1 = h[2 * pr + 1] * inv;
+              const uint16_t hp = pack_e4m3x2(x0, x1);
+              const float2 back = unpack_e4m3x2(hp);
+              const uint16_t lp = pack_e4m3x2(x0 - back.x, x1 - back.y);
+              hw[pr >> 1] |= static_cast<uint32_t>(hp) << (16 * (pr & 1));
+              lw[pr >> 1] |= static_cast<uint32_t>(lp) << (16 * (pr & 1));
+            }
+            const size_t off = orow * args.I + static_cast<size_t>(u.n) * kBlock + hc;
+            *reinterpret_cast<uint2*>(args.h_hi + off) = make_uint2(hw[0], hw[1]);
+            *reinterpret_cast<uint2*>(args.h_lo + off) = make_uint2(lw[0], lw[1]);
+            if (c == 0) args.h_scale_t[static_cast<size_t>(u.n) * cap + orow] = m / 448.0f;
+          }
+        } else {
+          // output columns oc + [0, 16) of the tile's 256
+          const int oc = c * 16;
+          const float* vp = xr + ((oc & 127) >> 6) * 128 + (oc >= 128 ? 64 : 0) + (oc & 63);
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            *reinterpret_cast<float4*>(v + j) = *reinterpret_cast<const float4*>(vp + j);
+          float m = 0.0f;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) m = fmaxf(m, fabsf(v[j]));
+#pragma unroll
+          for (int off = 8; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+          const int k = pow2_exponent_for_f16(m);
+          if (live) {
+            store_f16x16(v, ldexpf(1.0f, -k), args.y, orow, u.n * kTileN + oc, args.H);
+            if (c == 0) args.y_scale[orow * (args.H / kTileN) + u.n] = ldexpf(1.0f, k);
+          }
+        }
+        continue;
+      }
       if (KIND == 3) {
         // add the lo rows' sums to the hi rows' (same slot, same columns, same scales)
         const bool routed = prow < u.nrows;
