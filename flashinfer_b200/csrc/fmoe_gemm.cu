@@ -67,10 +67,10 @@ struct Cfg<2> {
 // GEMM2 for tiles of at most 64 routed slots (T <= kPackedMaxT): one A tile holds the hi term of
 // the tile's first 64 slots in rows 0-63 and their lo term in rows 64-127, so a K block takes
 // four MMAs instead of eight; at the tile end the lo rows' fp32 sums are added to the hi rows'
-// through shared memory (xbuf).
+// through shared memory (xbuf), 16 rows per round.
 template <>
 struct Cfg<3> {
-  static constexpr int NS = 3;
+  static constexpr int NS = 4;
   static constexpr int A_TILES = 1;
   static constexpr int STAGE = 128 * 128 * A_TILES + 256 * 128;  // 48 KB
 };
@@ -90,12 +90,12 @@ constexpr int kMaxKb = 64;  // K blocks per GEMM (H/128 and I/128); checked on t
 // group g at g * 128: its 64 first-half columns, then its 64 second-half columns), rows padded
 // by 4 floats (a warp's 16-byte accesses to consecutive rows then cover all 32 banks). It holds
 // the rows of a tile with at most kXSmall routed rows, which all epilogue threads then finish,
-// and for KIND 3 the lo rows of up to 64 slots.
+// and for KIND 3 the lo rows of 16 slots per exchange round.
 constexpr int kXRow = 2 * 128 + 4;
 constexpr int kXSmall = 16;
 template <int KIND>
 constexpr int xbuf_bytes() {
-  return (KIND == 3 ? 64 : kXSmall) * kXRow * 4;
+  return kXSmall * kXRow * 4;
 }
 
 struct alignas(16) GemmTail {
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   float* sa_ring = reinterpret_cast<float*>(smem + NS * STAGE);  // [kSaRing][128]
   GemmTail* tail = reinterpret_cast<GemmTail*>(smem + NS * STAGE + kSaRing * kSaBytes);
-  float* xbuf = reinterpret_cast<float*>(tail + 1);  // [kXSmall or 64][kXRow]
+  float* xbuf = reinterpret_cast<float*>(tail + 1);  // [kXSmall][kXRow]
   volatile int* abort_flag = &tail->abort_flag;
 
   const int warp = threadIdx.x >> 5;
@@ -639,24 +639,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       if (KIND == 3) {
-        // add the lo rows' sums to the hi rows' (same slot, same columns, same scales)
-        const bool routed = prow < u.nrows;
-        float4* x = reinterpret_cast<float4*>(xbuf + prow * kXRow + g * 128);
-        if (lo_row && routed) {
+        // add the lo rows' sums to the hi rows' (same slot, same columns, same scales), 16
+        // slots per round through xbuf
+        const int rounds = (u.nrows + kXSmall - 1) / kXSmall;
+        for (int rd = 0; rd < rounds; ++rd) {
+          const bool mine = prow >= rd * kXSmall && prow < (rd + 1) * kXSmall && prow < u.nrows;
+          float4* x = reinterpret_cast<float4*>(xbuf + (mine ? prow - rd * kXSmall : 0) * kXRow +
+                                                g * 128);
+          if (lo_row && mine) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i)
-            x[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
-        }
-        named_bar_sync(1, kEpiWarps * 32);
-        if (!lo_row && routed) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float4 v = x[i];
-            acc[4 * i] += v.x;
-            acc[4 * i + 1] += v.y;
-            acc[4 * i + 2] += v.z;
-            acc[4 * i + 3] += v.w;
+            for (int i = 0; i < 32; ++i)
+              x[i] = make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
           }
+          named_bar_sync(1, kEpiWarps * 32);
+          if (!lo_row && mine) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const float4 v = x[i];
+              acc[4 * i] += v.x;
+              acc[4 * i + 1] += v.y;
+              acc[4 * i + 2] += v.z;
+              acc[4 * i + 3] += v.w;
+            }
+          }
+          named_bar_sync(1, kEpiWarps * 32);  // xbuf is rewritten by the next round
         }
       }
       const bool valid = prow < u.nrows && !lo_row;
