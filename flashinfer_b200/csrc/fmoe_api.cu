@@ -68,6 +68,7 @@ struct DeviceInfo {
   int sms = 0;
   int major = 0;
   int minor = 0;
+  int device = -1;
 };
 
 int device_info(DeviceInfo* out) {
@@ -82,6 +83,7 @@ int device_info(DeviceInfo* out) {
         cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
         cudaDeviceGetAttribute(&d.minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
       return FMOE_ERR_CUDA;
+    d.device = dev;
     cache[dev] = d;
   }
   *out = cache[dev];
@@ -209,6 +211,65 @@ int fmoe_route(const void* logits, int32_t logits_dtype, const void* bias, int32
              : FMOE_ERR_CUDA;
 }
 
+}  // extern "C"
+
+namespace {
+
+// The GEMMs' seven TMA tensor maps depend only on the workspace and weight pointers and the
+// shapes; a call re-encodes them only when those change. Each host thread keeps the maps of its
+// last 16 argument sets (one per layer of a model, say), replaced round robin.
+struct TensorMaps {
+  CUtensorMap a, w1, hi, lo, w2, sa1, sa2;
+};
+
+struct TensorMapKey {
+  const void* ws;
+  const void* w1;
+  const void* w2;
+  int T, E, H, I, device;
+  bool operator==(const TensorMapKey& o) const {
+    return ws == o.ws && w1 == o.w1 && w2 == o.w2 && T == o.T && E == o.E && H == o.H &&
+           I == o.I && device == o.device;
+  }
+};
+
+constexpr int kTensorMapCache = 16;
+
+const TensorMaps* tensor_maps(const RunParams& p, const FmoeArgs* a, const Layout& L,
+                              int device) {
+  struct Entry {
+    bool valid;
+    TensorMapKey key;
+    TensorMaps maps;
+  };
+  thread_local Entry cache[kTensorMapCache] = {};
+  thread_local int next = 0;
+  const int T = p.T, E = p.E, H = p.H, I = p.I;
+  const TensorMapKey key{p.ws, a->gemm1_weights, a->gemm2_weights, T, E, H, I, device};
+  for (Entry& e : cache)
+    if (e.valid && e.key == key) return &e.maps;
+  Entry& e = cache[next];
+  e.valid = false;
+  TensorMaps* m = &e.maps;
+  if (!make_tmap_u8(&m->a, p.ws + L.a_perm, H, L.cap, H, 128, 128) ||
+      !make_tmap_u8(&m->w1, a->gemm1_weights, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128) ||
+      !make_tmap_u8(&m->hi, p.ws + L.h_hi, I, L.cap, I, 128, T <= kPackedMaxT ? 64 : 128) ||
+      !make_tmap_u8(&m->lo, p.ws + L.h_lo, I, L.cap, I, 128, T <= kPackedMaxT ? 64 : 128) ||
+      !make_tmap_u8(&m->w2, a->gemm2_weights, I, static_cast<uint64_t>(E) * H, I, 128, 256) ||
+      // per-K-block activation scales, [K blocks][cap] fp32: one 128-slot row per load
+      !make_tmap_f32_rows(&m->sa1, p.ws + L.a_scale_t, L.cap, H / kBlock, 128) ||
+      !make_tmap_f32_rows(&m->sa2, p.ws + L.h_scale_t, L.cap, I / kBlock, 128))
+    return nullptr;
+  e.key = key;
+  e.valid = true;
+  next = (next + 1) % kTensorMapCache;
+  return m;
+}
+
+}  // namespace
+
+extern "C" {
+
 int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   int rc = validate(a);
   if (rc) return rc;
@@ -260,16 +321,10 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   }
   if (a->stop_after == FMOE_STOP_ROUTE || a->stop_after == FMOE_STOP_GATHER) return FMOE_OK;
 
-  CUtensorMap tm_a, tm_w1, tm_hi, tm_lo, tm_w2, tm_sa1, tm_sa2;
-  if (!make_tmap_u8(&tm_a, p.ws + L.a_perm, H, L.cap, H, 128, 128) ||
-      !make_tmap_u8(&tm_w1, a->gemm1_weights, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128) ||
-      !make_tmap_u8(&tm_hi, p.ws + L.h_hi, I, L.cap, I, 128, T <= kPackedMaxT ? 64 : 128) ||
-      !make_tmap_u8(&tm_lo, p.ws + L.h_lo, I, L.cap, I, 128, T <= kPackedMaxT ? 64 : 128) ||
-      !make_tmap_u8(&tm_w2, a->gemm2_weights, I, static_cast<uint64_t>(E) * H, I, 128, 256) ||
-      // per-K-block activation scales, [K blocks][cap] fp32: one 128-slot row per load
-      !make_tmap_f32_rows(&tm_sa1, p.ws + L.a_scale_t, L.cap, H / kBlock, 128) ||
-      !make_tmap_f32_rows(&tm_sa2, p.ws + L.h_scale_t, L.cap, I / kBlock, 128))
-    return FMOE_ERR_CUDA;
+  const TensorMaps* tm = tensor_maps(p, a, L, d.device);
+  if (!tm) return FMOE_ERR_CUDA;
+  const CUtensorMap &tm_a = tm->a, &tm_w1 = tm->w1, &tm_hi = tm->hi, &tm_lo = tm->lo,
+                    &tm_w2 = tm->w2, &tm_sa1 = tm->sa1, &tm_sa2 = tm->sa2;
 
   if (launch_gemm1(p, tm_a, tm_w1, tm_sa1, s) != cudaSuccess) return FMOE_ERR_CUDA;
   if (T <= kSplitMaxT && launch_split_finish(p, 1, s) != cudaSuccess) return FMOE_ERR_CUDA;
