@@ -206,6 +206,33 @@ def time_calls(inputs, weights, local_start, rsf, n, phase=True):
     return ms, phases, out
 
 
+def time_graph(inputs, weights, local_start, rsf, n, reps=3):
+    """Mean ms per call of one CUDA graph of n calls (captured untimed), best of reps replays."""
+    lg, b, hs, sc = inputs
+    out = torch.empty((lg.shape[0], wl.HIDDEN), dtype=torch.bfloat16, device=lg.device)
+    launch(lg, b, hs, sc, *weights, local_start, rsf, out, None)  # workspace allocated outside
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream(lg.device)
+    cap.wait_stream(torch.cuda.current_stream(lg.device))
+    with torch.cuda.graph(g, stream=cap):
+        for _ in range(n):
+            launch(lg, b, hs, sc, *weights, local_start, rsf, out, None)
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(reps):
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        g.replay()
+        s1.record()
+        torch.cuda.synchronize()
+        best = min(best, s0.elapsed_time(s1) / n)
+    del g
+    return best
+
+
 def ctypes_array(events):
     import ctypes
     arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
@@ -281,12 +308,14 @@ def run_sweep(device, weights, peaks):
         ids, _ = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), cfg.rsf)
         acc = call_accounting(ids, 0, 32, cfg.T)
         time_calls(inp, weights, 0, cfg.rsf, 3, phase=False)
-        ms, _, _ = time_calls(inp, weights, 0, cfg.rsf, 20, phase=False)  # no inter-kernel events
-        _, ph, _ = time_calls(inp, weights, 0, cfg.rsf, 10)                # phase breakdown
+        ms_plain, _, _ = time_calls(inp, weights, 0, cfg.rsf, 20, phase=False)  # plain launches
+        ms = time_graph(inp, weights, 0, cfg.rsf, 20)                           # CUDA graph
+        _, ph, _ = time_calls(inp, weights, 0, cfg.rsf, 10)                     # phase breakdown
         us = ms * 1e3
         t_roof = max(acc["flops"] / (fp8_peak * 1e12), acc["bytes"] / (peaks["hbm_gbs"] * 1e9))
         rows.append({"config": name, "T": cfg.T, "P": acc["P"], "active_experts": acc["active_experts"],
-                     "us_per_call": round(us, 2), "tflops": round(acc["flops"] / (ms * 1e-3) / 1e12, 2),
+                     "us_per_call": round(us, 2), "us_per_call_plain_launches": round(ms_plain * 1e3, 2),
+                     "tflops": round(acc["flops"] / (ms * 1e-3) / 1e12, 2),
                      "hbm_tbs": round(acc["bytes"] / (ms * 1e-3) / 1e12, 3),
                      "roofline_us": round(t_roof * 1e6, 2), "roofline_frac": round(t_roof * 1e6 / us, 3),
                      "phase_us": [round(x * 1e3, 2) for x in ph]})
@@ -301,6 +330,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="t64_s4")
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="headline loop as plain launches instead of one CUDA graph of K calls")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="run warm-up calls plus one call of --workload on GPU 0 and exit "
@@ -329,20 +360,37 @@ def main():
 
     # warm-up, then EXACTLY K timed steps bracketed by barrier + synchronize. The headline loop
     # records no events between kernels (an event between two kernels breaks the programmatic
-    # dependent launch that overlaps their launch latency).
+    # dependent launch that overlaps their launch latency). By default the K calls are captured
+    # once, untimed, into one CUDA graph (kernel nodes keep their programmatic-dependency edges),
+    # and the timed region is one replay of it: K calls, no host launch overhead.
     time_calls(inp, weights, local_start, cfg.rsf, args.warmup, phase=False)
     out = torch.empty((cfg.T, wl.HIDDEN), dtype=torch.bfloat16, device=device)
     lg, b, hs, sc = inp
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        cap = torch.cuda.Stream(device)
+        cap.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(args.steps):
+                launch(lg, b, hs, sc, *weights, local_start, cfg.rsf, out, None)
+        torch.cuda.synchronize()
+        graph.replay()  # untimed: the first launch of a graph also uploads it to the device
+        torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(device.index or 0) as clocks:
         start.record()
-        for i in range(args.steps):
-            launch(lg, b, hs, sc, *weights, local_start, cfg.rsf, out, None)
+        if graph is not None:
+            graph.replay()
+        else:
+            for i in range(args.steps):
+                launch(lg, b, hs, sc, *weights, local_start, cfg.rsf, out, None)
         end.record()
         torch.cuda.synchronize()
     barrier(world)
+    del graph
     ms_local = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms_local, world)
 
@@ -407,6 +455,9 @@ def main():
                        "experts_global": 256, "experts_local": 32, "top_k": 8,
                        "P_rank0": acc["P"], "active_experts_rank0": acc["active_experts"],
                        "parallelism": f"expert-shard replicas x{world}",
+                       "launch": ("plain launches" if args.no_graph else
+                                  "one CUDA graph of the K calls (captured and first replayed "
+                                  "untimed), timed over one replay"),
                        "l2": "inputs larger than L2: each call streams "
                              f"{acc['active_experts'] * wl.bytes_per_expert() / 1e6:.0f} MB of weights"},
             "roofline": {"kernel": "k_gemm<1> (GEMM1 + SwiGLU)", "bound": "hbm",
