@@ -283,8 +283,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // The prologue and the weight loads of the first NS K iterations, which need nothing else,
   // run before the wait; the activations are loaded after it.
 
-  const int S = args.plan[KIND == 1 ? kPlanSplit1 : kPlanSplit2];
-  const int units = args.plan[KIND == 1 ? kPlanUnits1 : kPlanUnits2];
+  // Read through L2 (ld.global.cg): the plan kernel wrote these while lines of the previous
+  // call's tables may still sit in this SM's (non-coherent) L1.
+  const int S = __ldcg(args.plan + (KIND == 1 ? kPlanSplit1 : kPlanSplit2));
+  const int units = __ldcg(args.plan + (KIND == 1 ? kPlanUnits1 : kPlanUnits2));
   if (static_cast<int>(blockIdx.x) >= units) return;
 
   extern __shared__ uint8_t smem_raw[];
@@ -302,8 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int NT = KIND == 1 ? args.I / kBlock : args.H / kTileN;
 
   for (int i = threadIdx.x; i <= E; i += blockDim.x) {
-    tail->ebase[i] = args.expert_base[i];
-    if (i < E) tail->ecnt[i] = args.expert_count[i];
+    tail->ebase[i] = __ldcg(args.expert_base + i);
+    if (i < E) tail->ecnt[i] = __ldcg(args.expert_count + i);
   }
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < NS; ++s) {
