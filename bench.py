@@ -14,6 +14,7 @@ restatement (the oracle port; the reference itself is Triton-only) on the host c
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -22,6 +23,7 @@ import threading
 import time
 
 import numpy as np
+
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -299,6 +301,38 @@ def blas_threads() -> int:
         return os.cpu_count() or 1
 
 
+def quant_lines(device, peaks):
+    """Input quantisation kernel (bf16 -> e4m3 + per-128 scales) at the decode and the largest
+    prefill size: device time per call (CUDA events around 50 calls, inputs resident; at
+    T=16384 the 352 MB per call exceed L2) against the measured HBM copy bandwidth."""
+    rows = []
+    for T in (64, 16384):
+        g = torch.Generator().manual_seed(T)
+        x = torch.randn(T, wl.HIDDEN, generator=g).to(torch.bfloat16).to(device)
+        q = torch.empty((T, wl.HIDDEN), dtype=torch.uint8, device=device)
+        sc = torch.empty((wl.HIDDEN // 128, T), dtype=torch.float32, device=device)
+        lib = _lib.load()
+        args = (ctypes.c_void_p(x.data_ptr()), T, wl.HIDDEN, ctypes.c_void_p(q.data_ptr()),
+                ctypes.c_void_p(sc.data_ptr()),
+                ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream))
+        for _ in range(3):
+            assert lib.fmoe_quantize_activations(*args) == 0
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = 50
+        s0.record()
+        for _ in range(n):
+            lib.fmoe_quantize_activations(*args)
+        s1.record()
+        torch.cuda.synchronize()
+        us = s0.elapsed_time(s1) / n * 1e3
+        nbytes = T * (2 * wl.HIDDEN + wl.HIDDEN + 4 * (wl.HIDDEN // 128))
+        rows.append({"T": T, "us_per_call": round(us, 2), "bytes": nbytes,
+                     "gbs": round(nbytes / (us * 1e-6) / 1e9, 1),
+                     "frac_hbm": round(nbytes / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 3)})
+    return rows
+
+
 def run_sweep(device, weights, peaks):
     rows = []
     fp8_peak = 2.0 * peaks["bf16_tflops"]
@@ -482,6 +516,7 @@ def main():
         }
         if world == 1 and not args.no_sweep:
             result["sweep"] = run_sweep(device, weights, peaks)
+            result["input_quantization"] = quant_lines(device, peaks)
         if world == 1 and not args.no_cpu_baseline:
             ntok = 8
             secs = min(cpu_oracle_seconds(cfg, local_start, 32, ntok) for _ in range(2))

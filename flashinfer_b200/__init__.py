@@ -6,6 +6,6 @@ FlashInfer-Bench ``fused_moe`` solution
 path is hand-written CUDA behind the C ABI of ``include/fmoe.h``; expert
 parallelism over several GPUs is in ``flashinfer_b200.ep``.
 """
-from .moe import run, route, read_status, workspace_for, WorkspaceView  # noqa: F401
+from .moe import run, route, quantize_activations, read_status, workspace_for, WorkspaceView  # noqa: F401,E501
 
 __all__ = ["run", "route", "read_status", "workspace_for", "WorkspaceView"]

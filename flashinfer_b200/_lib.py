@@ -38,7 +38,7 @@ STATUS_TIMEOUT_GEMM2 = 0x2
 
 EXPORTS = ("fmoe_workspace_size", "fmoe_workspace_layout", "fmoe_run", "fmoe_route",
            "fmoe_read_status", "fmoe_device_sm_count", "fmoe_version",
-           "fmoe_route_permute_noalloc")
+           "fmoe_route_permute_noalloc", "fmoe_quantize_activations")
 
 
 class FmoeArgs(Structure):
@@ -105,6 +105,8 @@ def load() -> ctypes.CDLL:
                                                c_int32, c_int32, c_float, c_void_p, c_void_p,
                                                c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]
     lib.fmoe_device_sm_count.argtypes = [POINTER(c_int32)]
+    lib.fmoe_quantize_activations.argtypes = [c_void_p, c_int32, c_int32, c_void_p, c_void_p,
+                                              c_void_p]
     lib.fmoe_version.restype = c_char_p
     for name in EXPORTS:
         if name != "fmoe_version":

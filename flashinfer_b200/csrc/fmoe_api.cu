@@ -188,6 +188,28 @@ int fmoe_workspace_size(int32_t T, int32_t E, int32_t H, int32_t I, size_t* byte
   return FMOE_OK;
 }
 
+int fmoe_quantize_activations(const void* x, int32_t T, int32_t H, void* q, float* scale_t,
+                              void* stream) {
+  if (T < 0 || H <= 0 || H % kBlock != 0) return FMOE_ERR_SHAPE;
+  if (static_cast<int64_t>(T) * (H / kBlock) > (int64_t{1} << 30)) return FMOE_ERR_SHAPE;
+  if (T == 0) return FMOE_OK;
+  if (!x || !q || !scale_t) return FMOE_ERR_NULL;
+  if (!aligned16(x) || !aligned16(q) || !aligned16(scale_t)) return FMOE_ERR_ALIGN;
+  const auto lo = [](const void* p) { return reinterpret_cast<uintptr_t>(p); };
+  const uintptr_t xb = lo(x), xe = xb + static_cast<uintptr_t>(T) * H * 2;
+  const uintptr_t qb = lo(q), qe = qb + static_cast<uintptr_t>(T) * H;
+  const uintptr_t sb = lo(scale_t), se = sb + static_cast<uintptr_t>(T) * (H / kBlock) * 4;
+  if ((qb < xe && xb < qe) || (sb < xe && xb < se) || (sb < qe && qb < se)) return FMOE_ERR_SHAPE;
+  DeviceInfo d;
+  int rc = device_info(&d);
+  if (rc) return rc;
+  if (d.major != 10) return FMOE_ERR_DEVICE;
+  return launch_quantize_act(x, T, H, q, scale_t, d.sms, static_cast<cudaStream_t>(stream)) ==
+                 cudaSuccess
+             ? FMOE_OK
+             : FMOE_ERR_CUDA;
+}
+
 int fmoe_route(const void* logits, int32_t logits_dtype, const void* bias, int32_t bias_dtype,
                int32_t T, int32_t E_global, int32_t top_k, int32_t n_group, int32_t topk_group,
                float rsf, int32_t* topk_ids, float* topk_weights, void* stream) {

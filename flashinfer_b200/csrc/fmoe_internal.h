@@ -146,6 +146,9 @@ cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUte
 cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
                          const CUtensorMap& tm_w2, const CUtensorMap& tm_sa, cudaStream_t s);
 cudaError_t launch_combine(const RunParams& p, cudaStream_t s);
+// bf16 [T, H] -> e4m3 [T, H] + fp32 scales [H/128, T] (fmoe_quant.cu)
+cudaError_t launch_quantize_act(const void* x, int T, int H, void* q, float* scale_t,
+                                int num_sms, cudaStream_t s);
 
 // Routing + permutation with every buffer passed explicitly (used by the entry point whose
 // scratch lives in a statically allocated device array).

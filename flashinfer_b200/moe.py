@@ -183,6 +183,30 @@ def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor,
     return ids, w
 
 
+@torch.no_grad()
+def quantize_activations(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """bf16 activations [T, H] (CUDA, contiguous) -> (e4m3 [T, H], fp32 scales [H/128, T]).
+
+    The operator's input format: one scale per token and 128 columns, ``max(amax, 1e-30) / 448``,
+    and the values divided by it and rounded to the nearest e4m3 (ties to even). The scales come
+    transposed, as ``hidden_states_scale`` is consumed. Runs on the current stream.
+    """
+    if x.dim() != 2 or x.dtype != torch.bfloat16 or not x.is_cuda or not x.is_contiguous():
+        raise TypeError("x must be a contiguous CUDA bfloat16 tensor of shape [T, H]")
+    T, H = int(x.shape[0]), int(x.shape[1])
+    if H % BLOCK != 0:
+        raise ValueError(f"hidden size {H} is not a multiple of {BLOCK}")
+    q = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=x.device)
+    scale = torch.empty((H // BLOCK, T), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.load().fmoe_quantize_activations(
+            ctypes.c_void_p(x.data_ptr()), T, H, ctypes.c_void_p(q.data_ptr()),
+            ctypes.c_void_p(scale.data_ptr()),
+            ctypes.c_void_p(torch.cuda.current_stream(x.device).cuda_stream))
+    _lib.check(rc, "fmoe_quantize_activations")
+    return q, scale
+
+
 def read_status(workspace: torch.Tensor) -> int:
     """Device status word of the last call on this workspace (synchronises the stream)."""
     st = ctypes.c_int32(0)

@@ -189,6 +189,15 @@ FMOE_API int fmoe_route_permute_noalloc(const void* routing_logits, int32_t logi
                                         float* slot_weight, int32_t* token_slot,
                                         float* token_weight, void* cuda_stream);
 
+/* Input quantisation, the step that produces the operator's activation inputs: bf16
+ * x [T, H] (row-major, 16-byte aligned) -> e4m3 q [T, H] and fp32 scale_t [H/128, T], per token
+ * and 128-column block scale = max(amax, 1e-30) / 448, q = e4m3(x / scale) rounded to nearest
+ * even. No counterpart in the reference, which receives hidden_states already quantised in
+ * this layout (kernel.py:601-602; hidden_states_scale indexed [kb, token] at kernel.py:169).
+ * H must be a multiple of 128; q and scale_t must not overlap x. */
+FMOE_API int fmoe_quantize_activations(const void* x_bf16, int32_t num_tokens, int32_t hidden_size,
+                                       void* q_e4m3, float* scale_t, void* cuda_stream);
+
 /* Copies the device status word into *status (synchronises the stream). Non-zero means a
  * kernel gave up on a bounded wait and its outputs are not valid. */
 FMOE_API int fmoe_read_status(const void* workspace, void* cuda_stream, int32_t* status);

@@ -110,3 +110,28 @@ def test_two_term_intermediate_meets_tolerance(golden_outputs, cpu_weights):
     single = omoe.moe_device_numerics(hs, sc, W1, s1, W2, s2, ids, w, 0, two_term=False)
     frac1, _ = omoe.allclose_report(single, ref)
     assert frac1 < 0.95
+
+
+def _quant_inputs(T: int, H: int, seed: int) -> torch.Tensor:
+    """Seeded bf16 activations whose rows span 12 decades, with the edge blocks the quantiser
+    must handle: an all-zero block, a lone spike, negative zeros and bf16 subnormals."""
+    g = torch.Generator().manual_seed(seed)
+    mag = torch.pow(10.0, torch.empty(T, 1).uniform_(-6, 6, generator=g))
+    x = (torch.randn(T, H, generator=g) * mag).to(torch.bfloat16)
+    if T >= 4 and H >= 512:
+        x[0, :128] = 0.0
+        x[1, 128:256] = 0.0
+        x[1, 200] = -3.0e4
+        x[2, 256:384] = -0.0
+        x[3, 384:512] = torch.full((128,), 1.0e-39).to(torch.bfloat16)
+    return x
+
+
+def test_quant_oracle_matches_torch_cast():
+    """oracle/quant.py against torch's float8_e4m3fn conversion (the benchmark inputs' rule)."""
+    from oracle import quant as oquant
+    x = _quant_inputs(64, 1024, 3)
+    q_t, s_t = wl.quantize_activations(x)
+    q_o, s_o = oquant.quantize_activations(x.float().numpy())
+    np.testing.assert_array_equal(s_o.view(np.uint32), s_t.numpy().view(np.uint32))
+    np.testing.assert_array_equal(q_o, e4m3_to_f32(q_t.view(torch.uint8).numpy()))
