@@ -33,6 +33,9 @@ DTYPE_BF16 = 1
 OUT_BF16 = 0
 OUT_F32 = 1
 STOP_NONE, STOP_ROUTE, STOP_GATHER, STOP_GEMM1, STOP_GEMM2 = 0, 1, 2, 3, 4
+# FMOE_ROUTING_* (include/fmoe.h)
+(ROUTING_DEEPSEEK_V3, ROUTING_DEFAULT, ROUTING_RENORMALIZE, ROUTING_LLAMA4,
+ ROUTING_RENORMALIZE_NAIVE, ROUTING_TOPK) = range(6)
 STATUS_TIMEOUT_GEMM1 = 0x1
 STATUS_TIMEOUT_GEMM2 = 0x2
 
@@ -70,6 +73,7 @@ class FmoeArgs(Structure):
         ("phase_events", c_void_p),
         ("num_phase_events", c_int32),
         ("output_dtype", c_int32),
+        ("routing_method", c_int32),
     ]
 
 

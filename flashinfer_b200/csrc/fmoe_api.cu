@@ -104,9 +104,24 @@ int validate(const FmoeArgs* a) {
   int rc = check_sizes(a->num_tokens, a->num_local_experts, a->hidden_size,
                        a->intermediate_size);
   if (rc) return rc;
-  if (a->num_experts != kExpertsGlobal || a->top_k != kTopK || a->n_group != kGroups ||
-      a->topk_group != kTopKGroups)
-    return FMOE_ERR_SHAPE;
+  if (a->num_experts != kExpertsGlobal) return FMOE_ERR_SHAPE;
+  switch (a->routing_method) {
+    case FMOE_ROUTING_DEEPSEEK_V3:
+      if (a->top_k != kTopK || a->n_group != kGroups || a->topk_group != kTopKGroups)
+        return FMOE_ERR_SHAPE;
+      break;
+    case FMOE_ROUTING_LLAMA4:
+      if (a->top_k != 1) return FMOE_ERR_SHAPE;
+      break;
+    case FMOE_ROUTING_DEFAULT:
+    case FMOE_ROUTING_RENORMALIZE:
+    case FMOE_ROUTING_RENORMALIZE_NAIVE:
+    case FMOE_ROUTING_TOPK:
+      if (a->top_k < 1 || a->top_k > kTopK) return FMOE_ERR_SHAPE;
+      break;
+    default:
+      return FMOE_ERR_SHAPE;
+  }
   if (a->local_expert_offset < 0 ||
       a->local_expert_offset + a->num_local_experts > a->num_experts)
     return FMOE_ERR_OFFSET;
@@ -323,6 +338,7 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   p.E = E;
   p.local_start = a->local_expert_offset;
   p.rsf = a->routed_scaling_factor;
+  p.route_mode = route_mode(a->routing_method, a->top_k);
   p.ws = static_cast<uint8_t*>(a->workspace);
   p.L = L;
   p.num_sms = d.sms;

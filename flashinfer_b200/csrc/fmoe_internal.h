@@ -100,6 +100,10 @@ __host__ __device__ inline Layout make_layout(int T, int E, int H, int I) {
   return L;
 }
 
+// Routing method and top_k of a call, packed for the routing kernels: method | top_k << 8.
+__host__ __device__ constexpr int route_mode(int method, int top_k) { return method | (top_k << 8); }
+constexpr int kRouteDeepSeek = route_mode(FMOE_ROUTING_DEEPSEEK_V3, kTopK);
+
 struct RunParams {
   // inputs
   const void* logits;
@@ -114,6 +118,7 @@ struct RunParams {
   int out_f32;
   int T, H, I, E, local_start;
   float rsf;
+  int route_mode;              // route_mode(method, top_k)
   // workspace
   uint8_t* ws;
   Layout L;

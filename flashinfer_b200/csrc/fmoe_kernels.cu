@@ -53,9 +53,9 @@ __device__ __forceinline__ float sigmoid_rn(float x) {
 // Routes one token with one warp. Returns, in every lane, the 8 picks (selection order:
 // descending biased score, lowest index first on ties) and their weights.
 template <typename TL>
-__device__ __forceinline__ void route_token(const TL* __restrict__ row, const float (&b)[8],
-                                            float rsf, int lane, int (&ids)[kTopK],
-                                            float (&wts)[kTopK]) {
+__device__ __forceinline__ void route_token_ds(const TL* __restrict__ row, const float (&b)[8],
+                                               float rsf, int lane, int (&ids)[kTopK],
+                                               float (&wts)[kTopK]) {
   const float NEG_INF = -INFINITY;
   float x[8], s[8], sb[8];
   load8<TL>(row + lane * 8, x);
@@ -148,6 +148,132 @@ __device__ __forceinline__ void route_token(const TL* __restrict__ row, const fl
   for (int k = 0; k < kTopK; ++k) wts[k] = __shfl_sync(0xffffffffu, my_w, k);
 }
 
+// Order-preserving 32-bit key of a float (larger value, larger key; -0 and +0 equal).
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t u = __float_as_uint(v + 0.0f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// The other routing methods of the definition family (flashinfer/trace/templates/moe.py:
+// 187-390), one warp per token, lane l holding experts 8l..8l+7. z = logit + bias (fp32).
+// DEFAULT / RENORMALIZE_NAIVE select on softmax(z) (max-subtracted exponentials, expf, one
+// warp-wide sum, IEEE divide); RENORMALIZE, LLAMA4 and TOPK select on z. The top-K picks come
+// in descending order, ties to the lower expert index (one redux.sync max of the value's key,
+// a second for the index, per pick); picks k >= K are -1 with weight 0.
+template <typename TL>
+__device__ __forceinline__ void route_token_other(const TL* __restrict__ row, const float (&b)[8],
+                                                  float rsf, int method, int K, int lane,
+                                                  int (&ids)[kTopK], float (&wts)[kTopK]) {
+  float x[8], z[8], sel[8];
+  load8<TL>(row + lane * 8, x);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) z[i] = __fadd_rn(x[i], b[i]);
+  const bool softmax_first =
+      method == FMOE_ROUTING_DEFAULT || method == FMOE_ROUTING_RENORMALIZE_NAIVE;
+  if (softmax_first) {
+    float m = z[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, z[i]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float part = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sel[i] = expf(__fsub_rn(z[i], m));
+      part = __fadd_rn(part, sel[i]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, o));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sel[i] = __fdiv_rn(sel[i], part);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sel[i] = z[i];
+  }
+  uint32_t key[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) key[i] = order_key(sel[i]);
+  float pv[kTopK], pz[kTopK];  // each pick's selection value and its z
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) {
+    ids[k] = -1;
+    pv[k] = 0.0f;
+    pz[k] = 0.0f;
+    if (k >= K) continue;  // K is the same in every lane
+    uint32_t best = 0;
+    int bi = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (key[i] > best) {
+        best = key[i];
+        bi = i;
+      }
+    const uint32_t top = __reduce_max_sync(0xffffffffu, best);
+    const uint32_t mine = (best == top) ? static_cast<uint32_t>(255 - (lane * 8 + bi)) : 0u;
+    const int win = 255 - static_cast<int>(__reduce_max_sync(0xffffffffu, mine));
+    const int wl = win >> 3, wi = win & 7;
+    float v = 0.0f, zz = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i == wi) {
+        v = sel[i];
+        zz = z[i];
+      }
+    pv[k] = __shfl_sync(0xffffffffu, v, wl);
+    pz[k] = __shfl_sync(0xffffffffu, zz, wl);
+    ids[k] = win;
+    if (lane == wl) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i == wi) key[i] = 0u;
+    }
+  }
+  // weights (the same in every lane)
+  if (method == FMOE_ROUTING_DEFAULT) {
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) wts[k] = k < K ? __fmul_rn(pv[k], rsf) : 0.0f;
+  } else if (method == FMOE_ROUTING_RENORMALIZE_NAIVE) {
+    float sum = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k)
+      if (k < K) sum = __fadd_rn(sum, pv[k]);
+    sum = __fadd_rn(sum, 1e-20f);
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k)
+      wts[k] = k < K ? __fmul_rn(__fdiv_rn(pv[k], sum), rsf) : 0.0f;
+  } else if (method == FMOE_ROUTING_RENORMALIZE) {
+    float e[kTopK], sum = 0.0f;  // softmax over the picks; pz[0] is their maximum
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      e[k] = k < K ? expf(__fsub_rn(pz[k], pz[0])) : 0.0f;
+      if (k < K) sum = __fadd_rn(sum, e[k]);
+    }
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k)
+      wts[k] = k < K ? __fmul_rn(__fdiv_rn(e[k], sum), rsf) : 0.0f;
+  } else if (method == FMOE_ROUTING_LLAMA4) {
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) wts[k] = 0.0f;
+    wts[0] = __fmul_rn(__fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-pz[0]))), rsf);
+  } else {  // FMOE_ROUTING_TOPK
+    const float u = __fdiv_rn(rsf, static_cast<float>(K));
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) wts[k] = k < K ? u : 0.0f;
+  }
+}
+
+// Routes one token with one warp by the call's routing mode (route_mode(method, top_k)).
+template <typename TL>
+__device__ __forceinline__ void route_token(const TL* __restrict__ row, const float (&b)[8],
+                                            float rsf, int mode, int lane, int (&ids)[kTopK],
+                                            float (&wts)[kTopK]) {
+  const int method = mode & 0xff;
+  if (method == FMOE_ROUTING_DEEPSEEK_V3)
+    route_token_ds<TL>(row, b, rsf, lane, ids, wts);
+  else
+    route_token_other<TL>(row, b, rsf, method, mode >> 8, lane, ids, wts);
+}
+
 __device__ __forceinline__ void store_picks(int32_t* ids_out, float* w_out, int t,
                                             const int (&ids)[kTopK], const float (&w)[kTopK]) {
   int4* io = reinterpret_cast<int4*>(ids_out + static_cast<size_t>(t) * kTopK);
@@ -172,7 +298,8 @@ __global__ void __launch_bounds__(256) k_route(const TL* __restrict__ logits,
   for (int t = warp0; t < T; t += nwarps) {
     int ids[kTopK];
     float w[kTopK];
-    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, lane, ids, w);
+    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, kRouteDeepSeek,
+                    lane, ids, w);
     if (lane == 0) store_picks(ids_out, w_out, t, ids, w);
   }
 }
@@ -182,7 +309,7 @@ __global__ void __launch_bounds__(256) k_route(const TL* __restrict__ logits,
 template <typename TL, typename TB>
 __global__ void __launch_bounds__(256) k_route_hist(const TL* __restrict__ logits,
                                                     const TB* __restrict__ bias, int T, int tpb,
-                                                    float rsf, int local_start, int E,
+                                                    float rsf, int mode, int local_start, int E,
                                                     int32_t* __restrict__ ids_out,
                                                     float* __restrict__ w_out,
                                                     int32_t* __restrict__ block_hist) {
@@ -198,7 +325,8 @@ __global__ void __launch_bounds__(256) k_route_hist(const TL* __restrict__ logit
   for (int t = t0 + warp; t < t1; t += blockDim.x >> 5) {
     int ids[kTopK];
     float w[kTopK];
-    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, lane, ids, w);
+    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, mode, lane, ids,
+                    w);
     if (lane == 0) store_picks(ids_out, w_out, t, ids, w);
     if (lane < kTopK) {
       int mine = ids[0];
@@ -497,8 +625,8 @@ __global__ void __launch_bounds__(256) k_scatter(
 // slots are marked empty.
 template <typename TL, typename TB>
 __global__ void __launch_bounds__(32 * kSmallTokensPerCta) k_plan_small(
-    const TL* __restrict__ logits, const TB* __restrict__ bias, int T, float rsf, int local_start,
-    int E, int H, int I, int G, int allow_split, int32_t* __restrict__ ids_out,
+    const TL* __restrict__ logits, const TB* __restrict__ bias, int T, float rsf, int mode,
+    int local_start, int E, int H, int I, int G, int allow_split, int32_t* __restrict__ ids_out,
     float* __restrict__ w_out, int32_t* __restrict__ plan, int32_t* __restrict__ expert_count,
     int32_t* __restrict__ expert_base, int32_t* __restrict__ counters,
     int32_t* __restrict__ status, int32_t* __restrict__ slot_token,
@@ -527,7 +655,7 @@ __global__ void __launch_bounds__(32 * kSmallTokensPerCta) k_plan_small(
     load8<TB>(bias + lane * 8, b);
     int ids[kTopK];
     float w[kTopK];
-    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, lane, ids, w);
+    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, mode, lane, ids, w);
     if (lane == 0) {
       store_picks(ids_out, w_out, t, ids, w);
 #pragma unroll
@@ -684,7 +812,7 @@ cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s) {
     using TB = decltype(tb);
     (void)launch_pdl(k_route_hist<TL, TB>, L.nblocks, 256, 0, s,
         static_cast<const TL*>(p.logits), static_cast<const TB*>(p.bias), p.T, L.tpb, p.rsf,
-        p.local_start, p.E, reinterpret_cast<int32_t*>(ws + L.topk_ids),
+        p.route_mode, p.local_start, p.E, reinterpret_cast<int32_t*>(ws + L.topk_ids),
         reinterpret_cast<float*>(ws + L.topk_w), reinterpret_cast<int32_t*>(ws + L.block_hist));
     return cudaGetLastError();
   });
@@ -750,7 +878,8 @@ cudaError_t launch_plan_small(const RunParams& p, cudaStream_t s) {
                        : launch_pdl_cluster(kern, ncta, 32 * kSmallTokensPerCta, 0, s, ncta, a...);
     };
     (void)launch(static_cast<const TL*>(p.logits),
-                     static_cast<const TB*>(p.bias), p.T, p.rsf, p.local_start, p.E, p.H, p.I,
+                     static_cast<const TB*>(p.bias), p.T, p.rsf, p.route_mode, p.local_start,
+                     p.E, p.H, p.I,
                      p.num_sms, p.T <= kSplitMaxT ? 1 : 0,
                      reinterpret_cast<int32_t*>(ws + L.topk_ids),
                      reinterpret_cast<float*>(ws + L.topk_w), reinterpret_cast<int32_t*>(ws + L.plan),
@@ -778,7 +907,8 @@ cudaError_t launch_route_permute(const void* logits, int logits_dtype, const voi
     using TB = decltype(tb);
     (void)launch_pdl(k_route_hist<TL, TB>, nblocks, 256, 0, s, static_cast<const TL*>(logits),
                                                   static_cast<const TB*>(bias), T, tpb, rsf,
-                                                  local_start, E, bf.topk_ids, bf.topk_w,
+                                                  kRouteDeepSeek, local_start, E, bf.topk_ids,
+                                                  bf.topk_w,
                                                   bf.block_hist);
     return cudaGetLastError();
   });

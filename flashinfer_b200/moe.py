@@ -64,7 +64,8 @@ def workspace_for(device: torch.device, T: int, e_local: int, hidden: int, inter
 def _launch(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
             gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
             routed_scaling_factor, output, stop_after: int = _lib.STOP_NONE,
-            workspace: Optional[torch.Tensor] = None):
+            workspace: Optional[torch.Tensor] = None,
+            routing_method: int = _lib.ROUTING_DEEPSEEK_V3, top_k: int = TOP_K):
     T = int(routing_logits.shape[0])
     e_local = int(gemm1_weights.shape[0])
     hidden = int(hidden_states.shape[1])
@@ -116,7 +117,7 @@ def _launch(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
         a.intermediate_size = inter
         a.num_experts = E_GLOBAL
         a.num_local_experts = e_local
-        a.top_k = TOP_K
+        a.top_k = int(top_k)
         a.n_group = N_GROUP
         a.topk_group = TOPK_GROUP
         a.local_expert_offset = int(local_expert_offset)
@@ -125,6 +126,7 @@ def _launch(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
         a.workspace_bytes = ws.numel()
         a.stop_after = int(stop_after)
         a.output_dtype = _lib.OUT_F32 if output.dtype == torch.float32 else _lib.OUT_BF16
+        a.routing_method = int(routing_method)
         rc = _lib.load().fmoe_run(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream))
     _lib.check(rc, "fmoe_run")
     return output, ws, lay
@@ -135,7 +137,8 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
         hidden_states_scale: torch.Tensor, gemm1_weights: torch.Tensor,
         gemm1_weights_scale: torch.Tensor, gemm2_weights: torch.Tensor,
         gemm2_weights_scale: torch.Tensor, local_expert_offset: int,
-        routed_scaling_factor: float, output: Optional[torch.Tensor] = None) -> torch.Tensor:
+        routed_scaling_factor: float, output: Optional[torch.Tensor] = None, *,
+        routing_method: int = _lib.ROUTING_DEEPSEEK_V3, top_k: int = TOP_K) -> torch.Tensor:
     """Fused FP8 block-scale MoE with DeepSeek-V3 routing (reference ``kernel.py:600``).
 
     Tensor contract (all CUDA, contiguous):
@@ -150,10 +153,16 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
       output               bf16             [T, H]  (written in place; allocated if None)
     Experts [local_expert_offset, local_expert_offset + E_local) are local; the output holds
     the routing-weighted sum of the local experts only, like the reference.
+
+    Keyword-only, beyond the reference's signature: ``routing_method`` (``_lib.ROUTING_*``) picks
+    another routing of the same definition family (softmax/top-k variants, Llama4 top-1,
+    uniform top-k; ``include/fmoe.h`` lists them) with ``top_k`` experts per token (1..8;
+    DeepSeek-V3 uses 8, Llama4 1).
     """
     out, _, _ = _launch(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                         gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
-                        local_expert_offset, routed_scaling_factor, output)
+                        local_expert_offset, routed_scaling_factor, output,
+                        routing_method=routing_method, top_k=top_k)
     return out
 
 

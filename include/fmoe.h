@@ -57,6 +57,24 @@ extern "C" {
 #define FMOE_DTYPE_F32   0
 #define FMOE_DTYPE_BF16  1
 
+/* Routing methods (FmoeArgs.routing_method). DeepSeek-V3 is the hot path of kernel.py:371-457
+ * and the zero value; the others are the same definition family's routing references
+ * (flashinfer/trace/templates/moe.py:187-390; their RoutingMethodType number in brackets), all
+ * with routing_bias added to the logits first:
+ *   DEFAULT [0]            softmax -> top_k; weight = softmax value * rsf
+ *   RENORMALIZE [1]        top_k of the logits -> softmax over the picks * rsf
+ *   LLAMA4 [3]             top-1 of the logits; weight = sigmoid(logit) * rsf (top_k = 1)
+ *   RENORMALIZE_NAIVE [4]  softmax -> top_k -> divided by their sum (+1e-20) * rsf
+ *   TOPK [5]               top_k of the logits; every weight rsf / top_k
+ * Ties go to the lower expert index. top_k may be 1..8 except for DeepSeek-V3 (8) and
+ * Llama4 (1); n_group and topk_group are used by DeepSeek-V3 only. */
+#define FMOE_ROUTING_DEEPSEEK_V3       0
+#define FMOE_ROUTING_DEFAULT           1
+#define FMOE_ROUTING_RENORMALIZE       2
+#define FMOE_ROUTING_LLAMA4            3
+#define FMOE_ROUTING_RENORMALIZE_NAIVE 4
+#define FMOE_ROUTING_TOPK              5
+
 /* Stop points for staged execution (tests inspect the workspace in between). */
 #define FMOE_STOP_NONE     0
 #define FMOE_STOP_ROUTE    1   /* after routing, permutation and the activation gather */
@@ -108,6 +126,8 @@ typedef struct FmoeArgs {
    * in fp32, for callers that add several partial outputs (expert parallelism) before the
    * single final rounding to bf16. */
   int32_t output_dtype;
+  /* FMOE_ROUTING_*; 0 (DeepSeek-V3) for callers that zero the struct. */
+  int32_t routing_method;
 } FmoeArgs;
 
 /* Offsets (bytes from the workspace base) of the regions tests and tools read back. */

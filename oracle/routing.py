@@ -104,3 +104,53 @@ def permute(local_ids: np.ndarray, local_w: np.ndarray, e_local: int):
 def sorted_id_sets(ids: np.ndarray) -> np.ndarray:
     """Per-token ascending id sets (the torch reference's top-k order is unspecified)."""
     return np.sort(np.asarray(ids), axis=1)
+
+
+# The definition family's other routing methods (flashinfer/trace/templates/moe.py; the
+# numbers are FMOE_ROUTING_* of include/fmoe.h). Each starts from z = logits + bias in fp32.
+DEFAULT, RENORMALIZE, LLAMA4, RENORMALIZE_NAIVE, TOPK = 1, 2, 3, 4, 5
+
+
+def _softmax_f32(z: np.ndarray) -> np.ndarray:
+    m = z.max(axis=-1, keepdims=True)
+    e = np.exp((z - m).astype(F32)).astype(F32)
+    return (e / e.sum(axis=-1, keepdims=True, dtype=F32)).astype(F32)
+
+
+def route_method(logits: np.ndarray, bias: np.ndarray, rsf: float, method: int, top_k: int):
+    """Routing by ``method`` with ``top_k`` picks per token.
+
+    * DEFAULT (moe.py:205-209): s = softmax(z); the top_k of s; weight = s * rsf
+    * RENORMALIZE (moe.py:245-249): the top_k of z; weight = softmax over the picked z * rsf
+    * LLAMA4 (moe.py:285-288): argmax of z; weight = 1 / (1 + exp(-z)) * rsf (top_k = 1)
+    * RENORMALIZE_NAIVE (moe.py:321-326): s = softmax(z); the top_k of s;
+      weight = s / (their sum + 1e-20) * rsf
+    * TOPK (moe.py:370-378): the top_k of z; every weight rsf / top_k
+
+    Returns ``ids`` int32 ``[T, 8]`` in descending order of the selected value (ties to the
+    lowest index), -1 after ``top_k``, and ``weights`` fp32 ``[T, 8]`` (0 after ``top_k``).
+    """
+    z = (np.asarray(logits, dtype=F32) + np.asarray(bias, dtype=F32)[None, :]).astype(F32)
+    T = z.shape[0]
+    softmax_first = method in (DEFAULT, RENORMALIZE_NAIVE)
+    sel = _softmax_f32(z) if softmax_first else z
+    order = np.argsort(-sel, axis=1, kind="stable")[:, :top_k]
+    pv = np.take_along_axis(sel, order, axis=1).astype(F32)
+    pz = np.take_along_axis(z, order, axis=1).astype(F32)
+    if method == DEFAULT:
+        w = (pv * F32(rsf)).astype(F32)
+    elif method == RENORMALIZE_NAIVE:
+        w = (pv / (pv.sum(axis=1, keepdims=True, dtype=F32) + F32(1e-20)) * F32(rsf)).astype(F32)
+    elif method == RENORMALIZE:
+        w = (_softmax_f32(pz) * F32(rsf)).astype(F32)
+    elif method == LLAMA4:
+        w = (F32(1.0) / (F32(1.0) + np.exp(-pz).astype(F32)) * F32(rsf)).astype(F32)
+    elif method == TOPK:
+        w = np.full((T, top_k), F32(rsf) / F32(top_k), dtype=F32)
+    else:
+        raise ValueError(method)
+    ids = np.full((T, 8), -1, dtype=np.int32)
+    wts = np.zeros((T, 8), dtype=F32)
+    ids[:, :top_k] = order
+    wts[:, :top_k] = w
+    return ids, wts

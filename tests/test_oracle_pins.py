@@ -135,3 +135,55 @@ def test_quant_oracle_matches_torch_cast():
     q_o, s_o = oquant.quantize_activations(x.float().numpy())
     np.testing.assert_array_equal(s_o.view(np.uint32), s_t.numpy().view(np.uint32))
     np.testing.assert_array_equal(q_o, e4m3_to_f32(q_t.view(torch.uint8).numpy()))
+
+
+METHOD_CASES = [(1, 8), (1, 4), (2, 8), (2, 2), (3, 1), (4, 8), (4, 6), (5, 8), (5, 3)]
+
+
+def _reference_method_routing(logits: torch.Tensor, bias: torch.Tensor, rsf: float, method: int,
+                              top_k: int):
+    """The routing lines of the definition's references (flashinfer/trace/templates/moe.py:
+    205-209, 245-249, 285-288, 321-326, 370-378), in torch, as they are written there."""
+    lg = logits.to(torch.float32) + bias.to(torch.float32).reshape(-1)
+    if method == 1:
+        s = torch.softmax(lg, dim=-1)
+        _, idx = torch.topk(s, k=top_k, dim=1, largest=True, sorted=False)
+        w = s.gather(1, idx) * rsf
+    elif method == 2:
+        _, idx = torch.topk(lg, k=top_k, dim=1, largest=True, sorted=False)
+        w = torch.softmax(lg.gather(1, idx), dim=-1) * rsf
+    elif method == 3:
+        idx = lg.argmax(dim=-1, keepdim=True)
+        w = (1.0 / (1.0 + torch.exp(-lg.gather(1, idx)))) * rsf
+    elif method == 4:
+        s = torch.softmax(lg, dim=-1)
+        _, idx = torch.topk(s, k=top_k, dim=1, largest=True, sorted=False)
+        g = s.gather(1, idx)
+        w = g / (g.sum(dim=1, keepdim=True) + 1e-20) * rsf
+    else:
+        _, idx = torch.topk(lg, k=top_k, dim=1, largest=True, sorted=False)
+        w = torch.full((lg.shape[0], top_k), rsf / top_k, dtype=torch.float32)
+    return idx.numpy(), w.numpy()
+
+
+def _by_id(ids: np.ndarray, w: np.ndarray):
+    """Per token: (sorted ids, their weights) with the -1 padding dropped."""
+    out = []
+    for r in range(ids.shape[0]):
+        keep = ids[r] >= 0
+        o = np.argsort(ids[r][keep], kind="stable")
+        out.append((ids[r][keep][o], w[r][keep][o]))
+    return out
+
+
+@pytest.mark.parametrize("method,top_k", METHOD_CASES)
+def test_oracle_routing_methods_match_reference(method, top_k):
+    cfg = wl.CONFIGS["t64_s4"]
+    act = cfg.activations()
+    ids, w = orouting.route_method(act.routing_logits.numpy(), act.routing_bias.float().numpy(),
+                                   cfg.rsf, method, top_k)
+    rid, rw = _reference_method_routing(act.routing_logits, act.routing_bias, cfg.rsf, method,
+                                        top_k)
+    for (a_ids, a_w), (b_ids, b_w) in zip(_by_id(ids, w), _by_id(rid.astype(np.int32), rw)):
+        np.testing.assert_array_equal(a_ids, b_ids)
+        np.testing.assert_allclose(a_w, b_w, rtol=1e-6, atol=1e-9)
