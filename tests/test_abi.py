@@ -86,7 +86,16 @@ def test_bad_arguments_are_rejected_on_host():
     assert lib.fmoe_run(ctypes.byref(a), None) == -6
     a.logits_dtype = 0
     a.top_k = 6
-    assert lib.fmoe_run(ctypes.byref(a), None) == -2
+    assert lib.fmoe_run(ctypes.byref(a), None) == -2          # DeepSeek-V3 needs top_k 8
+    for method, top_k, rc in ((_lib.ROUTING_DEFAULT, 6, -1),   # valid: stops at the NULLs
+                              (_lib.ROUTING_TOPK, 1, -1),
+                              (_lib.ROUTING_LLAMA4, 2, -2),     # Llama4 is top-1
+                              (_lib.ROUTING_RENORMALIZE, 9, -2),
+                              (_lib.ROUTING_RENORMALIZE_NAIVE, 0, -2),
+                              (6, 8, -2)):                      # no such method
+        a.routing_method, a.top_k = method, top_k
+        assert lib.fmoe_run(ctypes.byref(a), None) == rc, (method, top_k)
+    a.routing_method, a.top_k = _lib.ROUTING_DEEPSEEK_V3, 8
     size = ctypes.c_size_t()
     assert lib.fmoe_workspace_size(16, 0, 7168, 2048, ctypes.byref(size)) == -2
     assert lib.fmoe_workspace_size(16, 32, 7168, 2048, None) == -1
