@@ -60,7 +60,8 @@ def measured_peaks():
 
 # ------------------------------------------------------------------------------- accounting
 def call_accounting(ids: np.ndarray, local_start: int, e_local: int, T: int):
-    """P, active experts, algorithmic FLOPs and bytes of one call (per SURVEY-style model)."""
+    """P, active experts, algorithmic FLOPs and bytes of one call (minimum traffic: the active
+    experts' weights and scales, the per-token inputs and output)."""
     loc = ids.astype(np.int64) - local_start
     hit = (loc >= 0) & (loc < e_local)
     P = int(hit.sum())
