@@ -6,18 +6,27 @@
 //   KIND 2  <- _persistent_gemm2_kernel kernel.py:193-293 (the reference runs this GEMM in
 //              TF32 on an fp32 intermediate; here A = hi + lo e4m3 terms, two MMAs per K block)
 //
-// Per CTA (persistent, one per SM, 352 threads):
-//   warps 0,10  TMA producers, alternating K iterations: A tile [128 slots x 128 K] (+ the lo
+// Per CTA (persistent, one per SM, 384 threads = three warpgroups):
+//   warps 0,2   TMA producers, alternating K iterations: A tile [128 slots x 128 K] (+ the lo
 //               term for KIND 2) and the weight tile [256 rows x 128 K] into an NS-stage
 //               shared-memory ring. One issuing warp sustains about 42 B/cycle per SM of
 //               128-row boxes; two sustain about 79 B/cycle, above the 48 KB per 520-cycle
 //               K block that the MMA consumes.
 //   warp 1      MMA issuer: per 128-wide K block, tcgen05.mma kind::f8f6f4 M=128 N=256 K=32
 //               x4 (x8 for KIND 2) into one of two TMEM partial buffers (2 x 256 columns).
-//   warps 2-9   promotion + epilogue: read each K block's partial from TMEM, scale it by
+//   warp 3      idle (completes warpgroup 0, whose register budget is handed to the epilogue).
+//   warps 4-11  promotion + epilogue: read each K block's partial from TMEM, scale it by
 //               a_scale[slot, kb] * w_scale[n-block, kb] and accumulate in fp32 registers
 //               with packed FMA (the reference's "partial * sa * sb" promotion,
 //               kernel.py:167-171).
+// After the prologue warpgroup 0 gives up registers (setmaxnreg.dec to 56) and the two
+// epilogue warpgroups take them (setmaxnreg.inc to 224): 168 x 384 = 56 x 128 + 224 x 256, so
+// each epilogue thread holds its 128 accumulators, two 16-column TMEM load buffers and the tile
+// end's working set without spilling in the K loop.
+// The hand-offs between the MMA warp and the epilogue are the pipeline's critical path (only two
+// 256-column TMEM buffers fit in TMEM): waits spin on mbarrier.test_wait (a suspended try_wait
+// wakes up late) and every epilogue lane arrives on the buffer-empty barrier itself (no warp
+// synchronisation before the arrive).
 // Work unit = (tile, K split). Tiles are ordered expert -> n-tile -> m-tile so concurrently
 // running CTAs share weight tiles in L2. For small batches with fewer tiles than SMs the K range
 // is split; every split writes its fp32 partial tile and k_split_finish (a separate kernel,
@@ -25,6 +34,8 @@
 // ever waits on another.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+
+#include <atomic>
 
 #include "fmoe_internal.h"
 #include "fmoe_ptx.cuh"
@@ -75,9 +86,14 @@ struct Cfg<3> {
   static constexpr int STAGE = 128 * 128 * A_TILES + 256 * 128;  // 48 KB
 };
 
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;
 constexpr int kEpiWarps = 8;
-constexpr int kProducer2Warp = 10;
+constexpr int kEpiWarp0 = 4;       // first epilogue warp (warpgroups 1 and 2)
+constexpr int kProducer2Warp = 2;
+constexpr int kRegsControl = 56;   // setmaxnreg of warpgroup 0 (producers, MMA)
+constexpr int kRegsEpilogue = 224; // setmaxnreg of the epilogue warpgroups
+static_assert(kRegsControl * 128 + kRegsEpilogue * 256 <= 168 * kThreads,
+              "register split exceeds the launch allocation (168 per thread at 384 threads)");
 constexpr int kTmemCols = 512;
 constexpr int kATileBytes = 128 * 128;
 // Activation scales of K iteration it land (by TMA, counted on full[s]) in ring entry it % 8.
@@ -157,15 +173,17 @@ __device__ __forceinline__ Unit decode_unit(int unit, int S, int NT, int nkb, co
   return u;
 }
 
-// Bounded wait that also gives up when another role of this CTA has already aborted.
+// Bounded wait that also gives up when another role of this CTA has already aborted. Spins on
+// the non-suspending test_wait: this wait sits on the MMA <-> epilogue hand-off, the pipeline's
+// critical path.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
                                               volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   uint32_t spins = 0;
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((++spins & 127u) == 0) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((++spins & 255u) == 0) {
       if (*abort_flag) return false;
       if (global_timer_ns() - t0 > FMOE_WAIT_NS) return false;
     }
@@ -314,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tail->tfull[b], 1);
-      mbar_init(&tail->tempty[b], kEpiWarps);
+      mbar_init(&tail->tempty[b], kEpiWarps * 32);  // every epilogue lane arrives
     }
     mbar_init(&tail->drain, 1);
     tail->abort_flag = 0;
@@ -348,18 +366,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                   u.e * args.H + u.n * kTileN, pol_w);
     }
   };
-  if ((warp == 0 || warp == kProducer2Warp) && lane == 0) {
-    const int pw = warp == 0 ? 0 : 1;
-    const uint64_t pol_w = policy_evict_first();
-    int it = 0;
-    for (int unit = blockIdx.x; unit < units && it < NS; unit += gridDim.x) {
-      const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
-      for (int kb = u.kb0; kb < u.kb1 && it < NS; ++kb, ++it)
-        if ((it & 1) == pw) issue_weights(it, u, kb, pol_w);
+  // Each role branch starts with its warpgroup's register change (ptxas allocates each branch
+  // under the limit its setmaxnreg sets), then waits for the previous grid.
+  if (warp < kEpiWarp0) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+    if ((warp == 0 || warp == kProducer2Warp) && lane == 0) {
+      const int pw = warp == 0 ? 0 : 1;
+      const uint64_t pol_w = policy_evict_first();
+      int it = 0;
+      for (int unit = blockIdx.x; unit < units && it < NS; unit += gridDim.x) {
+        const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
+        for (int kb = u.kb0; kb < u.kb1 && it < NS; ++kb, ++it)
+          if ((it & 1) == pw) issue_weights(it, u, kb, pol_w);
+      }
     }
-  }
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0 || warp == kProducer2Warp) {
     // ------------------------------------------------------------------ TMA producers
@@ -455,9 +477,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&tail->drain);
       (void)mbar_wait(&tail->drain, 0);
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsEpilogue));
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     // ------------------------------------------------------------------ promotion + epilogue
-    const int ew = warp - 2;
+    const int ew = warp - kEpiWarp0;
     const int g = ew >> 2;        // column group: 0 -> cols [0,64)+[128,192), 1 -> [64,128)+...
     const int q = warp & 3;       // TMEM lane quarter this warp may access
     const int r = q * 32 + lane;  // accumulator row owned by this thread
@@ -544,8 +570,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_before();
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tail->tempty[b]);
+        mbar_arrive(&tail->tempty[b]);
       }
       // w_sc[par ^ 1] was last read in the previous unit, which every epilogue thread has left
       if (has_next) store_w_scale(par ^ 1, w_next);
@@ -877,14 +902,16 @@ static cudaError_t launch_gemm_kind(const RunParams& p, const CUtensorMap& a0,
                                     const CUtensorMap& a1, const CUtensorMap& w,
                                     const CUtensorMap& sa, cudaStream_t s) {
   const size_t smem = gemm_smem_bytes<KIND>();
-  static int configured_device = -1;
+  // The shared-memory opt-in is a per-device function attribute: set once per device (an
+  // idempotent call, so two host threads that both see it unset only repeat it).
+  static std::atomic<bool> configured[64];
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (configured_device != dev) {
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!configured[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(k_gemm<KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          static_cast<int>(smem));
     if (e != cudaSuccess) return e;
-    configured_device = dev;
+    configured[dev].store(true, std::memory_order_release);
   }
   const GemmArgs a = gemm_args<KIND>(p);
   (void)launch_pdl(k_gemm<KIND>, p.num_sms, kThreads, smem, s, a0, a1, w, sa, a);

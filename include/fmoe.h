@@ -191,13 +191,18 @@ FMOE_API int fmoe_route(const void* routing_logits, int32_t logits_dtype, const 
  *
  * Writes the same tables fmoe_run() builds before its GEMMs: expert_count [E_local],
  * expert_base [E_local+1] (first slot of each expert, multiples of 128), slot_token and
- * slot_weight [cap] (cap = cap_slots of fmoe_workspace_layout; padding slots hold -1 / 0),
+ * slot_weight (the caller sizes them [cap], cap = cap_slots of fmoe_workspace_layout; only
+ * slots [0, expert_base[E_local]) are written -- the padding slots inside that range hold
+ * -1 / 0 -- and entries from expert_base[E_local] up to cap are left as the caller had them),
  * token_slot and token_weight [T, 8] (a token's local picks in ascending expert order, -1 /
  * 0 after them). Its scratch is one statically allocated device array of 336,384 bytes,
  * which every GPU that loads this library keeps until the process exits:
  *   - num_tokens may be at most 4096; larger requests return FMOE_ERR_NOALLOC_LIMIT;
  *   - the first call on a device looks up the array's device address (cudaGetSymbolAddress)
- *     with that device current; make that first call before any stream capture;
+ *     with that device current and keeps it for the life of the process; make that first
+ *     call before any stream capture, and do not use this entry point after a device reset
+ *     (cudaDeviceReset, or the primary context destroyed and re-created), which may move the
+ *     array;
  *   - all calls on a device share the array, so calls whose executions overlap on the GPU
  *     race and produce undefined tables: order them on one stream. */
 FMOE_API int fmoe_route_permute_noalloc(const void* routing_logits, int32_t logits_dtype,

@@ -34,6 +34,11 @@ def golden_outputs():
 
 
 @pytest.fixture(scope="session")
+def golden_sampled():
+    return np.load(os.path.join(GOLDEN, "sampled_rows.npz"))
+
+
+@pytest.fixture(scope="session")
 def cpu_weights():
     """All 32 local experts (offset 0), quantised on the CPU from their seeds."""
     from flashinfer_b200 import workload as wl
@@ -55,3 +60,16 @@ def oracle_weights_for(cpu_weights, experts):
     W1 = {e: w1[e].view(torch.uint8).numpy() for e in experts}
     W2 = {e: w2[e].view(torch.uint8).numpy() for e in experts}
     return W1, s1.numpy(), W2, s2.numpy()
+
+
+def bank_weights_for(experts):
+    """uint8/fp32 numpy views of the given GLOBAL experts' quantised weights (seeded per expert),
+    keyed by global expert id: the oracle's weight dicts for a local range starting at 0."""
+    import torch
+    from flashinfer_b200 import workload as wl
+    W1, S1, W2, S2 = {}, {}, {}, {}
+    for e in experts:
+        q1, s1, q2, s2 = wl.WeightBank.get(int(e))
+        W1[e], W2[e] = q1.view(torch.uint8).numpy(), q2.view(torch.uint8).numpy()
+        S1[e], S2[e] = s1.numpy(), s2.numpy()
+    return W1, S1, W2, S2

@@ -13,7 +13,16 @@ workloads of ``flashinfer_b200.workload`` on the CPU and records:
   (``moe.py:172-184``);
 * ``outputs.npz``  the reference's bf16 output rows (uint16 bit patterns) for the
   small configs (all rows for T <= 16, the first 16 rows for T = 64 and the
-  skewed T = 256 case).
+  skewed T = 256 case);
+* ``sampled_rows.npz`` the reference's bf16 output rows for a seeded sample of
+  tokens of every larger config (``SAMPLED``): tokens are independent (a token's
+  output depends only on its own logits row, activation row and the weights of
+  its picks), so the reference runs its routing on just those rows and then its
+  expert loop (``moe.py:28-100``) once per token over the token's own picks in
+  the config's local expert range -- the experts it needs, in a compact stack,
+  with the pick ids renumbered to index that stack. The expert-parallel configs
+  are recorded over all 256 experts (the sum every rank's partial adds up to).
+  ``python tests/golden/make_golden.py --sampled`` rebuilds only this file.
 
 Run it where the installed reference is importable (not needed on the GPU box):
 ``python tests/golden/make_golden.py``. Takes a few minutes on 8 cores.
@@ -38,6 +47,19 @@ EP_CONFIGS = {
     "ep_t16384_s11_hot": wl.Config("ep_t16384_s11_hot", 16384, 11, hot=1.5),
 }
 FULL_OUTPUT = {"t16_s0": None, "t1_s1": None, "t8_s2": None, "t64_s4": 16, "t256_s5_skew": 16}
+# Sampled-token golden rows: config -> (local expert range start, size, tokens to sample).
+SAMPLED = {
+    "t32_s3": (0, 32, 8), "t256_s5": (0, 32, 10), "t1024_s6": (0, 32, 12),
+    "t1024_s6_skew": (0, 32, 12), "t4096_s7": (0, 32, 12), "t8192_s8": (0, 32, 12),
+    "t16384_s9": (0, 32, 12), "ep_t16384_s10": (0, 256, 8), "ep_t16384_s11_hot": (0, 256, 8),
+}
+
+
+def sampled_tokens(cfg, n):
+    """The seeded token sample of a config: first, last and n more (sorted, distinct)."""
+    rng = np.random.default_rng(1000 + cfg.seed)
+    pick = rng.choice(cfg.T, size=min(cfg.T, n), replace=False)
+    return np.unique(np.concatenate([[0, cfg.T - 1], pick])).astype(np.int64)
 
 
 def reference_module():
@@ -69,8 +91,51 @@ def reference_routing(m, act, rsf):
     return np.take_along_axis(idx, order, 1), np.take_along_axis(w, order, 1)
 
 
+def reference_token_rows(m, act, rsf, tokens, local_start, e_local):
+    """Reference bf16 output rows (uint16 bits) of the given tokens, local experts only."""
+    sub = wl.Activations(act.routing_logits[tokens].contiguous(), act.routing_bias,
+                         act.hidden_states[tokens].contiguous(),
+                         act.hidden_states_scale[:, tokens].contiguous())
+    ids, w = reference_routing(m, sub, rsf)
+    rows = []
+    for i in range(len(tokens)):
+        mine = [int(e) for e in ids[i] if local_start <= int(e) < local_start + e_local]
+        if not mine:
+            rows.append(np.zeros(wl.HIDDEN, dtype=np.uint16))
+            continue
+        w1, s1, w2, s2 = wl.WeightBank.stacked(mine)
+        remap = {e: j for j, e in enumerate(mine)}
+        idx = torch.tensor([[remap.get(int(e), -1) for e in ids[i]]], dtype=torch.int64)
+        out = m._fp8_moe_run_experts(sub.hidden_states[i:i + 1], sub.hidden_states_scale[:, i:i + 1],
+                                     w1, s1, w2, s2, torch.from_numpy(w[i:i + 1].copy()), idx,
+                                     0, wl.E_GLOBAL)
+        rows.append(out.view(torch.int16).numpy().view(np.uint16)[0])
+    return np.stack(rows)
+
+
+def make_sampled(m):
+    all_cfgs = dict(wl.CONFIGS)
+    all_cfgs.update(EP_CONFIGS)
+    rows = {}
+    for name, (start, e_local, n) in SAMPLED.items():
+        cfg = all_cfgs[name]
+        act = cfg.activations()
+        tok = sampled_tokens(cfg, n)
+        t0 = time.time()
+        rows[f"{name}/tokens"] = tok
+        rows[f"{name}/out"] = reference_token_rows(m, act, cfg.rsf, tok, start, e_local)
+        print(name, "sampled rows", len(tok), f"{time.time() - t0:.1f}s", flush=True)
+        # each expert's weights are only needed by this config's sample
+        wl.WeightBank._cache.clear()
+    rows["meta/torch"] = np.array(torch.__version__)
+    np.savez_compressed(os.path.join(HERE, "sampled_rows.npz"), **rows)
+
+
 def main():
     torch.set_num_threads(os.cpu_count() or 8)
+    if "--sampled" in sys.argv:
+        make_sampled(reference_module())
+        return
     m = reference_module()
     routing = {}
     all_cfgs = dict(wl.CONFIGS)

@@ -15,8 +15,8 @@ from flashinfer_b200 import moe as fmoe
 from flashinfer_b200 import workload as wl
 from oracle import moe as omoe
 from oracle import routing as orouting
-from tests.conftest import oracle_weights_for
-from tests.golden.make_golden import EP_CONFIGS, FULL_OUTPUT
+from tests.conftest import bank_weights_for, oracle_weights_for
+from tests.golden.make_golden import EP_CONFIGS, FULL_OUTPUT, SAMPLED
 
 pytestmark = pytest.mark.gpu
 
@@ -125,7 +125,8 @@ def test_output_matches_oracle_and_golden(name, gpu_weights, cpu_weights, golden
     assert frac == 1.0, (frac, err)
 
 
-@pytest.mark.parametrize("name", ["t32_s3", "t256_s5", "t1024_s6_skew", "t4096_s7", "t16384_s9"])
+@pytest.mark.parametrize("name", ["t32_s3", "t256_s5", "t1024_s6", "t1024_s6_skew", "t4096_s7",
+                                  "t8192_s8", "t16384_s9"])
 def test_output_sampled_rows(name, gpu_weights, cpu_weights):
     """Large T: every token's output depends only on its own row and routing, so the oracle
     checks a seeded sample of rows (plus the first and last token)."""
@@ -140,6 +141,66 @@ def test_output_sampled_rows(name, gpu_weights, cpu_weights):
     frac, err = omoe.allclose_report(bits[sel], ref, atol=ATOL, rtol=RTOL)
     assert frac == 1.0, (frac, err)
     assert np.isfinite(out.float().cpu().numpy()).all()
+
+
+@pytest.mark.parametrize("name", sorted(n for n, v in SAMPLED.items() if v[1] == 32))
+def test_output_matches_reference_golden_rows(name, gpu_weights, golden_sampled):
+    """Every larger single-GPU config against the reference's own output rows (sampled tokens,
+    produced by tests/golden/make_golden.py from the operator's PyTorch definition)."""
+    cfg = wl.CONFIGS[name]
+    act = cfg.activations()
+    out, _, _ = run_gpu(act, gpu_weights, cfg)
+    bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
+    tok = golden_sampled[f"{name}/tokens"]
+    frac, err = omoe.allclose_report(bits[tok], golden_sampled[f"{name}/out"], atol=ATOL, rtol=RTOL)
+    assert frac == 1.0, (frac, err)
+
+
+def _weights_256(experts):
+    """Stacked weights of all 256 experts on the GPU, with the seeded values for ``experts`` and
+    zeros elsewhere (only the tokens whose picks are all in ``experts`` are checked)."""
+    H, I = wl.HIDDEN, wl.INTER
+    dev = torch.device("cuda:0")
+    w1 = torch.zeros((256, 2 * I, H), dtype=torch.uint8, device=dev)
+    s1 = torch.zeros((256, 2 * I // 128, H // 128), dtype=torch.float32, device=dev)
+    w2 = torch.zeros((256, H, I), dtype=torch.uint8, device=dev)
+    s2 = torch.zeros((256, H // 128, I // 128), dtype=torch.float32, device=dev)
+    for e in experts:
+        q1, a1, q2, a2 = wl.WeightBank.get(int(e))
+        w1[e].copy_(q1.view(torch.uint8))
+        s1[e].copy_(a1)
+        w2[e].copy_(q2.view(torch.uint8))
+        s2[e].copy_(a2)
+    return (w1.view(torch.float8_e4m3fn), s1, w2.view(torch.float8_e4m3fn), s2)
+
+
+@pytest.mark.parametrize("name", sorted(EP_CONFIGS))
+def test_all_256_experts_on_one_gpu(name, golden_sampled):
+    """configs[4]'s global batch (T=16384) with all 256 experts local on one GPU -- the
+    single-GPU point of the expert-parallel scaling run -- against the reference's rows and the
+    oracle for the sampled tokens."""
+    cfg = EP_CONFIGS[name]
+    act = cfg.activations()
+    tok = golden_sampled[f"{name}/tokens"]
+    ids, w = orouting.route(act.routing_logits.numpy()[tok], act.routing_bias.float().numpy(),
+                            cfg.rsf)
+    need = sorted({int(e) for e in ids.reshape(-1)})
+    weights = _weights_256(need)
+    out, _, _ = run_gpu(act, weights, cfg)
+    bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
+    frac, err = omoe.allclose_report(bits[tok], golden_sampled[f"{name}/out"], atol=ATOL, rtol=RTOL)
+    assert frac == 1.0, (frac, err)
+    W1, S1, W2, S2 = bank_weights_for(need)
+
+    class Dense(dict):
+        def __len__(self):
+            return 256
+
+    ref = omoe.moe_reference(act.hidden_states.view(torch.uint8).numpy()[tok],
+                             act.hidden_states_scale.numpy()[:, tok], W1, Dense(S1), W2,
+                             Dense(S2), ids, w, 0)
+    frac, err = omoe.allclose_report(bits[tok], ref, atol=ATOL, rtol=RTOL)
+    assert frac == 1.0, (frac, err)
 
 
 def test_deterministic_bits(gpu_weights):

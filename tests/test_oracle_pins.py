@@ -12,8 +12,8 @@ from flashinfer_b200 import workload as wl
 from oracle import moe as omoe
 from oracle import routing as orouting
 from oracle.fp8 import bf16_round, bf16_to_f32, e4m3_to_f32, round_e4m3
-from tests.conftest import oracle_weights_for
-from tests.golden.make_golden import EP_CONFIGS, FULL_OUTPUT
+from tests.conftest import bank_weights_for, oracle_weights_for
+from tests.golden.make_golden import EP_CONFIGS, FULL_OUTPUT, SAMPLED
 
 ALL = dict(wl.CONFIGS)
 ALL.update(EP_CONFIGS)
@@ -70,6 +70,38 @@ def test_oracle_forward_matches_reference(name, golden_outputs, cpu_weights):
     frac, maxerr = omoe.allclose_report(got, ref, atol=1e-5, rtol=2.0 ** -7)
     assert frac == 1.0, (frac, maxerr)
     assert np.mean(got == ref) > 0.99
+
+
+class _DenseScales(dict):
+    """Per-expert scale lookup that reports the local range size (the oracle takes len())."""
+
+    def __init__(self, d, n):
+        super().__init__(d)
+        self.n = n
+
+    def __len__(self):
+        return self.n
+
+
+@pytest.mark.parametrize("name", ["t1024_s6_skew", "t16384_s9", "ep_t16384_s10"])
+def test_oracle_matches_reference_sampled_rows(name, golden_sampled):
+    """The oracle against the reference's own output rows for sampled tokens of large configs
+    (the first three sampled tokens; the expert-parallel config over all 256 experts)."""
+    cfg = ALL[name]
+    start, e_local, _ = SAMPLED[name]
+    tok = golden_sampled[f"{name}/tokens"][:3]
+    gold = golden_sampled[f"{name}/out"][:3]
+    act = cfg.activations()
+    ids, w = orouting.route(act.routing_logits.numpy()[tok], act.routing_bias.float().numpy(),
+                            cfg.rsf)
+    need = sorted({int(e) for e in ids.reshape(-1) if start <= e < start + e_local})
+    W1, S1, W2, S2 = bank_weights_for(need)
+    hs = act.hidden_states.view(torch.uint8).numpy()[tok]
+    sc = act.hidden_states_scale.numpy()[:, tok]
+    got = omoe.moe_reference(hs, sc, W1, _DenseScales(S1, e_local), W2, _DenseScales(S2, e_local),
+                             ids, w, start)
+    frac, maxerr = omoe.allclose_report(got, gold, atol=1e-5, rtol=2.0 ** -7)
+    assert frac == 1.0, (frac, maxerr)
 
 
 def test_e4m3_codec_roundtrip():

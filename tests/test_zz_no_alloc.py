@@ -42,6 +42,17 @@ def _noalloc(act, rsf, local_start, e_local, cap):
     return out
 
 
+def _route_only_weights(e_local):
+    """Weight tensors of the right shapes for a call that stops after the permutation (their
+    contents are never read before that stop point)."""
+    dev = torch.device("cuda:0")
+    H, I = wl.HIDDEN, wl.INTER
+    return (torch.empty((e_local, 2 * I, H), dtype=torch.float8_e4m3fn, device=dev),
+            torch.empty((e_local, 2 * I // 128, H // 128), dtype=torch.float32, device=dev),
+            torch.empty((e_local, H, I), dtype=torch.float8_e4m3fn, device=dev),
+            torch.empty((e_local, H // 128, I // 128), dtype=torch.float32, device=dev))
+
+
 def _workspace_tables(act, rsf, local_start, gpu_weights):
     dev = torch.device("cuda:0")
     w1, s1, w2, s2 = gpu_weights
@@ -74,16 +85,37 @@ def test_noalloc_tables_match_workspace_entry_point(gpu_weights):
         cases.append((name, cfg, act, local_start, ref, cap, padded))
     results = [_noalloc(act, cfg.rsf, ls, 32, cap) for _, cfg, act, ls, _, cap, _ in cases]
     for (name, cfg, act, local_start, ref, cap, padded), got in zip(cases, results):
-        for key in ("expert_count", "expert_base", "token_slot"):
-            assert torch.equal(got[key], ref[key]), (name, key)
-        assert torch.equal(got["slot_token"][:padded], ref["slot_token"]), name
-        # fp32 weights are copied, not recomputed differently: compare their bits
-        assert torch.equal(got["slot_weight"][:padded].view(torch.int32),
-                           ref["slot_weight"].view(torch.int32)), name
-        assert torch.equal(got["token_weight"].view(torch.int32),
-                           ref["token_weight"].view(torch.int32)), name
-        # nothing written past the padded slot range
-        assert torch.all(got["slot_token"][padded:] == -7)
+        _check(name, ref, got, padded)
+
+
+def _check(name, ref, got, padded):
+    for key in ("expert_count", "expert_base", "token_slot"):
+        assert torch.equal(got[key], ref[key]), (name, key)
+    assert torch.equal(got["slot_token"][:padded], ref["slot_token"]), name
+    # fp32 weights are copied, not recomputed differently: compare their bits
+    assert torch.equal(got["slot_weight"][:padded].view(torch.int32),
+                       ref["slot_weight"].view(torch.int32)), name
+    assert torch.equal(got["token_weight"].view(torch.int32),
+                       ref["token_weight"].view(torch.int32)), name
+    # nothing written past the padded slot range
+    assert torch.all(got["slot_token"][padded:] == -7), name
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("e_local", [32, 256])
+def test_noalloc_at_its_token_limit(e_local):
+    """The largest accepted call (T = 4096: the top-k regions of the scratch are filled exactly;
+    with 256 local experts the per-block histogram reaches its 8192-count capacity), then a
+    T = 4095 call right after it on the same stream, both against the workspace tables."""
+    weights = _route_only_weights(e_local)
+    cases = []
+    for T, seed in ((_lib.NOALLOC_MAX_TOKENS, 41), (_lib.NOALLOC_MAX_TOKENS - 1, 42)):
+        act = wl.make_activations(T, seed)
+        ref, cap, padded = _workspace_tables(act, wl.RSF_DEFAULT, 0, weights)
+        cases.append((T, act, ref, cap, padded))
+    results = [_noalloc(act, wl.RSF_DEFAULT, 0, e_local, cap) for _, act, _, cap, _ in cases]
+    for (T, act, ref, cap, padded), got in zip(cases, results):
+        _check(f"T={T} E={e_local}", ref, got, padded)
 
 
 def test_noalloc_rejects_more_tokens_than_its_scratch_holds():
