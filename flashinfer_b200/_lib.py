@@ -11,9 +11,10 @@ import ctypes
 import os
 from ctypes import POINTER, Structure, byref, c_char_p, c_float, c_int32, c_int64, c_size_t, c_void_p
 
-# FLASHINFER_B200_LIB points at another build of the same library (A/B timing of two builds).
-LIB_PATH = os.environ.get("FLASHINFER_B200_LIB") or os.path.join(
-    os.path.dirname(os.path.abspath(__file__)), "_lib", "libfmoe.so")
+# FLASHINFER_B200_LIB points at another build of the same library (A/B timing of two builds);
+# a process that loads one says so on stderr, so a run on another build never passes unnoticed.
+DEFAULT_LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib", "libfmoe.so")
+LIB_PATH = os.environ.get("FLASHINFER_B200_LIB") or DEFAULT_LIB_PATH
 
 FMOE_OK = 0
 ERRORS = {
@@ -32,6 +33,14 @@ DTYPE_F32 = 0
 DTYPE_BF16 = 1
 OUT_BF16 = 0
 OUT_F32 = 1
+OUT_F16S = 2
+EP_MAX_RANKS = 8
+
+
+def ep_row_bytes(hidden: int) -> int:
+    """FMOE_EP_ROW_BYTES: an fp16 partial row plus its power-of-two scale per 256 columns,
+    padded to a multiple of 32 bytes."""
+    return (hidden * 2 + hidden // 256 * 4 + 31) // 32 * 32
 STOP_NONE, STOP_ROUTE, STOP_GATHER, STOP_GEMM1, STOP_GEMM2 = 0, 1, 2, 3, 4
 # FMOE_ROUTING_* (include/fmoe.h)
 (ROUTING_DEEPSEEK_V3, ROUTING_DEFAULT, ROUTING_RENORMALIZE, ROUTING_LLAMA4,
@@ -41,7 +50,9 @@ STATUS_TIMEOUT_GEMM2 = 0x2
 
 EXPORTS = ("fmoe_workspace_size", "fmoe_workspace_layout", "fmoe_run", "fmoe_route",
            "fmoe_read_status", "fmoe_device_sm_count", "fmoe_version",
-           "fmoe_route_permute_noalloc", "fmoe_quantize_activations")
+           "fmoe_route_permute_noalloc", "fmoe_quantize_activations", "fmoe_ep_layout",
+           "fmoe_ep_alloc", "fmoe_ep_free", "fmoe_ipc_get_handle", "fmoe_ipc_open",
+           "fmoe_ipc_close", "fmoe_ep_dispatch", "fmoe_ep_reduce", "fmoe_fp8_mma_peak")
 
 
 class FmoeArgs(Structure):
@@ -74,7 +85,18 @@ class FmoeArgs(Structure):
         ("num_phase_events", c_int32),
         ("output_dtype", c_int32),
         ("routing_method", c_int32),
+        ("topk_ids", c_void_p),
+        ("topk_weights", c_void_p),
+        ("region_counts", c_void_p),
+        ("region_tokens", c_int32),
+        ("region_output", c_void_p * EP_MAX_RANKS),
     ]
+
+
+class FmoeEpLayout(Structure):
+    _fields_ = [(n, c_size_t) for n in ("total_bytes", "recv_hidden", "recv_scale", "recv_ids",
+                                        "recv_weights", "recv_counts", "ret_rows")] + \
+        [("cap", c_int64), ("row_bytes", c_size_t)]
 
 
 class FmoeLayout(Structure):
@@ -98,6 +120,10 @@ def load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
             f"{LIB_PATH} is missing: build the CUDA library with `python -m flashinfer_b200.build`")
+    if LIB_PATH != DEFAULT_LIB_PATH:
+        import sys
+        print(f"flashinfer_b200: loading {LIB_PATH} (FLASHINFER_B200_LIB), not the in-tree build",
+              file=sys.stderr)
     lib = ctypes.CDLL(LIB_PATH)
     lib.fmoe_workspace_size.argtypes = [c_int32, c_int32, c_int32, c_int32, POINTER(c_size_t)]
     lib.fmoe_workspace_layout.argtypes = [c_int32, c_int32, c_int32, c_int32, POINTER(FmoeLayout)]
@@ -111,6 +137,17 @@ def load() -> ctypes.CDLL:
     lib.fmoe_device_sm_count.argtypes = [POINTER(c_int32)]
     lib.fmoe_quantize_activations.argtypes = [c_void_p, c_int32, c_int32, c_void_p, c_void_p,
                                               c_void_p]
+    lib.fmoe_ep_layout.argtypes = [c_int32, c_int32, c_int32, POINTER(FmoeEpLayout)]
+    lib.fmoe_ep_alloc.argtypes = [c_size_t, POINTER(c_void_p)]
+    lib.fmoe_ep_free.argtypes = [c_void_p]
+    lib.fmoe_ipc_get_handle.argtypes = [c_void_p, c_void_p]
+    lib.fmoe_ipc_open.argtypes = [c_void_p, POINTER(c_void_p)]
+    lib.fmoe_ipc_close.argtypes = [c_void_p]
+    lib.fmoe_ep_dispatch.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+                                     c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p]
+    lib.fmoe_ep_reduce.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
+                                   c_void_p, c_void_p]
+    lib.fmoe_fp8_mma_peak.argtypes = [c_int32, c_void_p, POINTER(ctypes.c_double), c_void_p]
     lib.fmoe_version.restype = c_char_p
     for name in EXPORTS:
         if name != "fmoe_version":
@@ -127,4 +164,10 @@ def check(rc: int, what: str) -> None:
 def workspace_layout(T: int, e_local: int, hidden: int, inter: int) -> FmoeLayout:
     lay = FmoeLayout()
     check(load().fmoe_workspace_layout(T, e_local, hidden, inter, byref(lay)), "fmoe_workspace_layout")
+    return lay
+
+
+def ep_layout(world: int, capacity: int, hidden: int) -> FmoeEpLayout:
+    lay = FmoeEpLayout()
+    check(load().fmoe_ep_layout(world, capacity, hidden, byref(lay)), "fmoe_ep_layout")
     return lay

@@ -64,6 +64,24 @@ bool make_tmap_u8(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 4-D uint8 tensor map over the weights for the GEMMs' half tiles: dims {cols, rows_per_block,
+// 2, outer} with strides {cols, rows_per_block * cols, 2 * rows_per_block * cols} bytes (a plain
+// reshape of the row-major weights, no overlap), box {128, 64, 2, 1}, 128-byte swizzle: one load
+// gives rows [r, r+64) of two consecutive blocks as one 128-row K-major tile.
+bool make_tmap_u8_halves(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows_per_block,
+                         uint64_t outer) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[4] = {cols, rows_per_block, 2, outer};
+  const cuuint64_t strides[3] = {cols, rows_per_block * cols, 2 * rows_per_block * cols};
+  const cuuint32_t box[4] = {128, 64, 2, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 struct DeviceInfo {
   int sms = 0;
   int major = 0;
@@ -125,19 +143,38 @@ int validate(const FmoeArgs* a) {
   if (a->local_expert_offset < 0 ||
       a->local_expert_offset + a->num_local_experts > a->num_experts)
     return FMOE_ERR_OFFSET;
-  if ((a->logits_dtype != FMOE_DTYPE_F32 && a->logits_dtype != FMOE_DTYPE_BF16) ||
-      (a->bias_dtype != FMOE_DTYPE_F32 && a->bias_dtype != FMOE_DTYPE_BF16) ||
-      (a->output_dtype != FMOE_OUT_BF16 && a->output_dtype != FMOE_OUT_F32))
+  const bool pre_routed = a->topk_ids != nullptr;
+  if ((!pre_routed && ((a->logits_dtype != FMOE_DTYPE_F32 && a->logits_dtype != FMOE_DTYPE_BF16) ||
+                       (a->bias_dtype != FMOE_DTYPE_F32 && a->bias_dtype != FMOE_DTYPE_BF16))) ||
+      (a->output_dtype != FMOE_OUT_BF16 && a->output_dtype != FMOE_OUT_F32 &&
+       a->output_dtype != FMOE_OUT_F16S))
     return FMOE_ERR_DTYPE;
+  // partial rows and token regions only for pre-routed calls (the receiving side of expert
+  // parallelism); regions must tile the tokens, at most one per rank
+  if (a->output_dtype == FMOE_OUT_F16S && !pre_routed) return FMOE_ERR_DTYPE;
+  if (a->region_counts != nullptr &&
+      (!pre_routed || a->region_tokens <= 0 || a->num_tokens % a->region_tokens != 0 ||
+       a->num_tokens / a->region_tokens > FMOE_EP_MAX_RANKS))
+    return FMOE_ERR_SHAPE;
   if (a->num_tokens == 0) return FMOE_OK;
-  const void* ptrs[] = {a->routing_logits, a->routing_bias,        a->hidden_states,
-                        a->hidden_states_scale, a->gemm1_weights,  a->gemm1_weights_scale,
-                        a->gemm2_weights,       a->gemm2_weights_scale, a->output,
+  const void* ptrs[] = {pre_routed ? a->topk_ids : a->routing_logits,
+                        pre_routed ? static_cast<const void*>(a->topk_weights) : a->routing_bias,
+                        a->hidden_states, a->hidden_states_scale, a->gemm1_weights,
+                        a->gemm1_weights_scale, a->gemm2_weights, a->gemm2_weights_scale,
+                        a->output_dtype == FMOE_OUT_F16S ? a->region_output[0] : a->output,
                         a->workspace};
   for (const void* p : ptrs)
     if (!p) return FMOE_ERR_NULL;
   for (const void* p : ptrs)
     if (!aligned16(p)) return FMOE_ERR_ALIGN;
+  if (a->output_dtype == FMOE_OUT_F16S) {
+    const int regions = a->region_counts ? a->num_tokens / a->region_tokens : 1;
+    for (int r = 0; r < regions; ++r) {
+      if (!a->region_output[r]) return FMOE_ERR_NULL;
+      // rows are written with 32-byte stores (FMOE_EP_ROW_BYTES is a multiple of 32)
+      if ((reinterpret_cast<uintptr_t>(a->region_output[r]) & 31u) != 0) return FMOE_ERR_ALIGN;
+    }
+  }
   return FMOE_OK;
 }
 
@@ -289,10 +326,12 @@ const TensorMaps* tensor_maps(const RunParams& p, const FmoeArgs* a, const Layou
   e.valid = false;
   TensorMaps* m = &e.maps;
   if (!make_tmap_u8(&m->a, p.ws + L.a_perm, H, L.cap, H, 128, 128) ||
-      !make_tmap_u8(&m->w1, a->gemm1_weights, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128) ||
+      // W1 [E][2][I][H]: {K, row in gate/up block, block, expert}
+      !make_tmap_u8_halves(&m->w1, a->gemm1_weights, H, I, E) ||
       !make_tmap_u8(&m->hi, p.ws + L.h_hi, I, L.cap, I, 128, T <= kPackedMaxT ? 64 : 128) ||
       !make_tmap_u8(&m->lo, p.ws + L.h_lo, I, L.cap, I, 128, T <= kPackedMaxT ? 64 : 128) ||
-      !make_tmap_u8(&m->w2, a->gemm2_weights, I, static_cast<uint64_t>(E) * H, I, 128, 256) ||
+      // W2 [E*H/256][2][128][I]: {K, row in n-block, n-block, 256-row tile}
+      !make_tmap_u8_halves(&m->w2, a->gemm2_weights, I, 128, static_cast<uint64_t>(E) * H / 256) ||
       // per-K-block activation scales, [K blocks][cap] fp32: one 128-slot row per load
       !make_tmap_f32_rows(&m->sa1, p.ws + L.a_scale_t, L.cap, H / kBlock, 128) ||
       !make_tmap_f32_rows(&m->sa2, p.ws + L.h_scale_t, L.cap, I / kBlock, 128))
@@ -331,7 +370,6 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   p.w1_scale = a->gemm1_weights_scale;
   p.w2_scale = a->gemm2_weights_scale;
   p.output = a->output;
-  p.out_f32 = a->output_dtype == FMOE_OUT_F32;
   p.T = T;
   p.H = H;
   p.I = I;
@@ -339,6 +377,12 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   p.local_start = a->local_expert_offset;
   p.rsf = a->routed_scaling_factor;
   p.route_mode = route_mode(a->routing_method, a->top_k);
+  p.in_ids = a->topk_ids;
+  p.in_w = a->topk_weights;
+  p.region_counts = a->region_counts;
+  p.region_tokens = a->region_counts ? a->region_tokens : T;
+  p.out_mode = a->output_dtype;
+  for (int r = 0; r < FMOE_EP_MAX_RANKS; ++r) p.region_out[r] = a->region_output[r];
   p.ws = static_cast<uint8_t*>(a->workspace);
   p.L = L;
   p.num_sms = d.sms;
@@ -349,7 +393,12 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   };
   if (!mark(0)) return FMOE_ERR_CUDA;
   // The plan kernel (k_scan or k_plan_small) clears the status word before any GEMM can set it.
-  if (T <= kSmallT) {
+  if (p.in_ids != nullptr) {
+    // pre-routed: the given picks replace the routing; the permutation is the same
+    if (launch_hist_given(p, s) != cudaSuccess || launch_scan(p, s) != cudaSuccess || !mark(1))
+      return FMOE_ERR_CUDA;
+    if (launch_scatter_gather(p, s) != cudaSuccess || !mark(2)) return FMOE_ERR_CUDA;
+  } else if (T <= kSmallT) {
     if (launch_plan_small(p, s) != cudaSuccess || !mark(1)) return FMOE_ERR_CUDA;
     if (launch_gather(p, s) != cudaSuccess || !mark(2)) return FMOE_ERR_CUDA;
   } else {

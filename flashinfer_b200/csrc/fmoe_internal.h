@@ -114,11 +114,17 @@ struct RunParams {
   const float* hidden_scale;   // [H/128, T]
   const float* w1_scale;       // [E, 2I/128, H/128]
   const float* w2_scale;       // [E, H/128, I/128]
-  void* output;                // [T, H] bf16, or fp32 when out_f32
-  int out_f32;
+  void* output;                // [T, H] bf16, or fp32 (out_mode FMOE_OUT_F32)
   int T, H, I, E, local_start;
   float rsf;
   int route_mode;              // route_mode(method, top_k)
+  // pre-routed call (expert parallelism): picks given, optional regions of valid tokens
+  const int32_t* in_ids;       // [T, 8] global ids or nullptr
+  const float* in_w;           // [T, 8]
+  const int32_t* region_counts;
+  int region_tokens;
+  int out_mode;                // FMOE_OUT_*
+  void* region_out[FMOE_EP_MAX_RANKS];
   // workspace
   uint8_t* ws;
   Layout L;
@@ -151,6 +157,9 @@ cudaError_t launch_gemm1(const RunParams& p, const CUtensorMap& tm_a, const CUte
 cudaError_t launch_gemm2(const RunParams& p, const CUtensorMap& tm_hi, const CUtensorMap& tm_lo,
                          const CUtensorMap& tm_w2, const CUtensorMap& tm_sa, cudaStream_t s);
 cudaError_t launch_combine(const RunParams& p, cudaStream_t s);
+// pre-routed: copies the given picks into the workspace (-1 for tokens outside their region's
+// count) with the per-block histogram, in place of launch_route_hist
+cudaError_t launch_hist_given(const RunParams& p, cudaStream_t s);
 // bf16 [T, H] -> e4m3 [T, H] + fp32 scales [H/128, T] (fmoe_quant.cu)
 cudaError_t launch_quantize_act(const void* x, int T, int H, void* q, float* scale_t,
                                 int num_sms, cudaStream_t s);

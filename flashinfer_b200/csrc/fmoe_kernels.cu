@@ -11,6 +11,8 @@
 #include <cuda_fp16.h>
 #include <math.h>
 
+#include <type_traits>
+
 #include "fmoe_internal.h"
 #include "fmoe_ptx.cuh"
 
@@ -335,6 +337,57 @@ __global__ void __launch_bounds__(256) k_route_hist(const TL* __restrict__ logit
         if (lane == k) mine = ids[k];
       const int le = mine - local_start;
       if (le >= 0 && le < E) atomicAdd(&hist[le], 1);
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    block_hist[static_cast<size_t>(blockIdx.x) * E + e] = hist[e];
+}
+
+// Pre-routed calls (expert parallelism): the picks come from the sending rank's routing. Block
+// b copies its tokens' picks into the workspace tables -- a token outside its region's count
+// gets no picks (-1 / 0) -- and counts its local picks per expert, like k_route_hist.
+__global__ void __launch_bounds__(256) k_hist_given(const int32_t* __restrict__ in_ids,
+                                                    const float* __restrict__ in_w,
+                                                    const int32_t* __restrict__ region_counts,
+                                                    int region_tokens, int T, int tpb,
+                                                    int local_start, int E,
+                                                    int32_t* __restrict__ ids_out,
+                                                    float* __restrict__ w_out,
+                                                    int32_t* __restrict__ block_hist) {
+  __shared__ int hist[kMaxLocalExperts];
+  pdl_begin();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+  __syncthreads();
+  const int t0 = blockIdx.x * tpb;
+  const int t1 = min(T, t0 + tpb);
+  for (int t = t0 + static_cast<int>(threadIdx.x); t < t1; t += blockDim.x) {
+    bool valid = true;
+    if (region_counts != nullptr) {
+      const int r = t / region_tokens;
+      valid = t - r * region_tokens < __ldg(region_counts + r);
+    }
+    const int4* ip = reinterpret_cast<const int4*>(in_ids + static_cast<size_t>(t) * kTopK);
+    const float4* wp = reinterpret_cast<const float4*>(in_w + static_cast<size_t>(t) * kTopK);
+    int4 i0 = make_int4(-1, -1, -1, -1), i1 = i0;
+    float4 w0 = make_float4(0.f, 0.f, 0.f, 0.f), w1 = w0;
+    if (valid) {
+      i0 = __ldg(ip);
+      i1 = __ldg(ip + 1);
+      w0 = __ldg(wp);
+      w1 = __ldg(wp + 1);
+    }
+    int4* io = reinterpret_cast<int4*>(ids_out + static_cast<size_t>(t) * kTopK);
+    float4* wo = reinterpret_cast<float4*>(w_out + static_cast<size_t>(t) * kTopK);
+    io[0] = i0;
+    io[1] = i1;
+    wo[0] = w0;
+    wo[1] = w1;
+    const int ids[kTopK] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      const int le = ids[k] - local_start;
+      if (ids[k] >= 0 && le >= 0 && le < E) atomicAdd(&hist[le], 1);
     }
   }
   __syncthreads();
@@ -818,6 +871,18 @@ cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s) {
   });
 }
 
+cudaError_t launch_hist_given(const RunParams& p, cudaStream_t s) {
+  if (p.T <= 0) return cudaSuccess;
+  uint8_t* ws = p.ws;
+  const Layout& L = p.L;
+  (void)launch_pdl(k_hist_given, L.nblocks, 256, 0, s, p.in_ids, p.in_w, p.region_counts,
+                   p.region_tokens, p.T, L.tpb, p.local_start, p.E,
+                   reinterpret_cast<int32_t*>(ws + L.topk_ids),
+                   reinterpret_cast<float*>(ws + L.topk_w),
+                   reinterpret_cast<int32_t*>(ws + L.block_hist));
+  return cudaGetLastError();
+}
+
 cudaError_t launch_scan(const RunParams& p, cudaStream_t s) {
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
@@ -950,12 +1015,53 @@ __device__ __forceinline__ void store8(float* out, size_t v, const float (&acc)[
 constexpr int kCombineVec = 4;
 constexpr int kCombineThreads = 128;
 
+// Destinations of FMOE_OUT_F16S rows: token t = r * region_tokens + j goes to p[r] + j * rowbytes.
+struct RegionOut {
+  void* p[FMOE_EP_MAX_RANKS];
+};
+
+// Exponent k of the smallest 2^k with amax / 2^k <= 16384: fp16 range kept, scaling exact.
+__device__ __forceinline__ int pow2_exp_f16(float amax) {
+  int ex = 0;
+  const float m = frexpf(amax, &ex);
+  return (m > 0.5f ? ex : ex - 1) - 14;
+}
+
+// One 32-column piece of a partial row: fp16 values with the 256-column block's power-of-two
+// scale (the block's 8 owning threads, consecutive lanes, agree on it by a shuffle reduction).
+__device__ __forceinline__ void store_f16s(uint8_t* row, int H, int col0, unsigned mask,
+                                           const float (&acc)[kCombineVec][8]) {
+  float m = 0.0f;
+#pragma unroll
+  for (int k = 0; k < kCombineVec; ++k)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = fmaxf(m, fabsf(acc[k][i]));
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) m = fmaxf(m, __shfl_xor_sync(mask, m, o));
+  const int e = pow2_exp_f16(m);
+  const float inv = ldexpf(1.0f, -e);
+  uint32_t w[2][8];
+#pragma unroll
+  for (int k = 0; k < kCombineVec; ++k)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2 h = __floats2half2_rn(acc[k][2 * i] * inv, acc[k][2 * i + 1] * inv);
+      w[k >> 1][(k & 1) * 4 + i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+  st_global_v8(row + static_cast<size_t>(col0) * 2, w[0]);
+  st_global_v8(row + static_cast<size_t>(col0) * 2 + 32, w[1]);
+  if ((col0 & (kTileN - 1)) == 0)
+    reinterpret_cast<float*>(row + static_cast<size_t>(H) * 2)[col0 / kTileN] = ldexpf(1.0f, e);
+}
+
 template <typename TOut>
 __global__ void __launch_bounds__(kCombineThreads) k_combine(const int32_t* __restrict__ token_slot,
                                                              const float* __restrict__ token_weight,
                                                              const __half* __restrict__ y,
                                                              const float* __restrict__ y_scale,
-                                                             int T, int H, TOut* __restrict__ out) {
+                                                             int T, int H, TOut* __restrict__ out,
+                                                             const RegionOut regions,
+                                                             int region_tokens) {
   pdl_begin();
   const int nvec = H / 8;
   const int ntile = H / kTileN;
@@ -973,6 +1079,8 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(const int32_t* __re
     const int slots[kTopK] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
     const float w[kTopK] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
     if (v0 >= nvec) continue;
+    // partial rows: a token without a local pick was not received (its row is not written)
+    if (std::is_same<TOut, uint8_t>::value && slots[0] < 0) continue;
     const int col0 = v0 * 8;  // 32 columns: two 32-byte loads of the y row
     const int tile = col0 / kTileN;
     float acc[kCombineVec][8];
@@ -1000,8 +1108,19 @@ __global__ void __launch_bounds__(kCombineThreads) k_combine(const int32_t* __re
         }
       }
     }
+    if constexpr (std::is_same<TOut, uint8_t>::value) {
+      // the 8 threads of a 256-column block are consecutive lanes with the same token, and a
+      // token's threads are all active or all skipped: the shuffle mask is the lane's octet
+      const unsigned mask = 0xffu << (threadIdx.x & 24);
+      const int r = t / region_tokens;
+      uint8_t* row = static_cast<uint8_t*>(regions.p[r]) +
+                     static_cast<size_t>(t - r * region_tokens) * FMOE_EP_ROW_BYTES(H);
+      store_f16s(row, H, col0, mask, acc);
+    } else {
 #pragma unroll
-    for (int k = 0; k < kCombineVec; ++k) store8(out + static_cast<size_t>(t) * H, v0 + k, acc[k]);
+      for (int k = 0; k < kCombineVec; ++k)
+        store8(out + static_cast<size_t>(t) * H, v0 + k, acc[k]);
+    }
   }
 }
 
@@ -1012,19 +1131,22 @@ cudaError_t launch_combine(const RunParams& p, cudaStream_t s) {
   const int per_block = kCombineThreads * kCombineVec;
   const long work = static_cast<long>(p.T) * ((p.H / 8 + per_block - 1) / per_block);
   const int blocks = static_cast<int>(work < p.num_sms * 16L ? work : p.num_sms * 16L);
-  if (p.out_f32)
-    (void)launch_pdl(k_combine<float>, blocks, kCombineThreads, 0, s, reinterpret_cast<const int32_t*>(ws + L.token_slot),
-                                            reinterpret_cast<const float*>(ws + L.token_weight),
-                                            reinterpret_cast<const __half*>(ws + L.y_rows),
-                                            reinterpret_cast<const float*>(ws + L.y_scale), p.T,
-                                            p.H, static_cast<float*>(p.output));
+  RegionOut regions{};
+  for (int r = 0; r < FMOE_EP_MAX_RANKS; ++r) regions.p[r] = p.region_out[r];
+  const int rt = p.region_tokens > 0 ? p.region_tokens : p.T;
+  const auto* ts = reinterpret_cast<const int32_t*>(ws + L.token_slot);
+  const auto* tw = reinterpret_cast<const float*>(ws + L.token_weight);
+  const auto* yr = reinterpret_cast<const __half*>(ws + L.y_rows);
+  const auto* ys = reinterpret_cast<const float*>(ws + L.y_scale);
+  if (p.out_mode == FMOE_OUT_F32)
+    (void)launch_pdl(k_combine<float>, blocks, kCombineThreads, 0, s, ts, tw, yr, ys, p.T, p.H,
+                     static_cast<float*>(p.output), regions, rt);
+  else if (p.out_mode == FMOE_OUT_F16S)
+    (void)launch_pdl(k_combine<uint8_t>, blocks, kCombineThreads, 0, s, ts, tw, yr, ys, p.T, p.H,
+                     static_cast<uint8_t*>(nullptr), regions, rt);
   else
-    (void)launch_pdl(k_combine<__nv_bfloat16>, blocks, kCombineThreads, 0, s,
-        reinterpret_cast<const int32_t*>(ws + L.token_slot),
-        reinterpret_cast<const float*>(ws + L.token_weight),
-        reinterpret_cast<const __half*>(ws + L.y_rows),
-        reinterpret_cast<const float*>(ws + L.y_scale), p.T, p.H,
-        static_cast<__nv_bfloat16*>(p.output));
+    (void)launch_pdl(k_combine<__nv_bfloat16>, blocks, kCombineThreads, 0, s, ts, tw, yr, ys, p.T,
+                     p.H, static_cast<__nv_bfloat16*>(p.output), regions, rt);
   return cudaGetLastError();
 }
 

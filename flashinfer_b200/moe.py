@@ -13,7 +13,7 @@ device allocation once the per-stream workspace exists, and no CPU fallback.
 from __future__ import annotations
 
 import ctypes
-from typing import Dict, Optional, Tuple
+from typing import Dict, Optional, Sequence, Tuple
 
 import torch
 
@@ -164,6 +164,95 @@ def run(routing_logits: torch.Tensor, routing_bias: torch.Tensor, hidden_states:
                         local_expert_offset, routed_scaling_factor, output,
                         routing_method=routing_method, top_k=top_k)
     return out
+
+
+@torch.no_grad()
+def run_routed(topk_ids: torch.Tensor, topk_weights: torch.Tensor, hidden_states: torch.Tensor,
+               hidden_states_scale: torch.Tensor, gemm1_weights: torch.Tensor,
+               gemm1_weights_scale: torch.Tensor, gemm2_weights: torch.Tensor,
+               gemm2_weights_scale: torch.Tensor, local_expert_offset: int,
+               output: Optional[torch.Tensor] = None, *,
+               region_counts: Optional[torch.Tensor] = None, region_tokens: int = 0,
+               region_output: Optional[Sequence[int]] = None,
+               workspace: Optional[torch.Tensor] = None,
+               phase_events: Optional[Sequence[torch.cuda.Event]] = None):
+    """The operator on tokens routed elsewhere: the receiving side of expert parallelism.
+
+    ``topk_ids`` int32 [T, 8] holds GLOBAL expert ids (-1 = no pick) and ``topk_weights`` fp32
+    [T, 8] their routing weights, as the sending rank's routing produced them; the local experts
+    are [local_expert_offset, local_expert_offset + E_local). With ``region_counts`` (int32 [R],
+    on the device) the T tokens are R regions of ``region_tokens`` and token j of region r takes
+    part only if j < region_counts[r]. ``output`` is bf16 or fp32 [T, H]; or, with
+    ``region_output`` (R device addresses), each taking-part token's partial row is written as
+    fp16 + power-of-two scales to region_output[r] + j * FMOE_EP_ROW_BYTES(H) (the address may be
+    another GPU's memory mapped into this process) and nothing is returned. ``phase_events``
+    (six CUDA events) are recorded at the operator's phase boundaries (``FmoeArgs.phase_events``).
+    """
+    T = int(topk_ids.shape[0])
+    e_local = int(gemm1_weights.shape[0])
+    hidden = int(hidden_states.shape[1])
+    inter = int(gemm2_weights.shape[2])
+    _expect(topk_ids, "topk_ids", (T, TOP_K), torch.int32)
+    _expect(topk_weights, "topk_weights", (T, TOP_K), torch.float32)
+    _expect(hidden_states, "hidden_states", (T, hidden), torch.float8_e4m3fn)
+    _expect(hidden_states_scale, "hidden_states_scale", (hidden // BLOCK, T), torch.float32)
+    _expect(gemm1_weights, "gemm1_weights", (e_local, 2 * inter, hidden), torch.float8_e4m3fn)
+    _expect(gemm1_weights_scale, "gemm1_weights_scale",
+            (e_local, 2 * inter // BLOCK, hidden // BLOCK), torch.float32)
+    _expect(gemm2_weights, "gemm2_weights", (e_local, hidden, inter), torch.float8_e4m3fn)
+    _expect(gemm2_weights_scale, "gemm2_weights_scale",
+            (e_local, hidden // BLOCK, inter // BLOCK), torch.float32)
+    device = hidden_states.device
+    if region_output is None:
+        if output is None:
+            output = torch.empty((T, hidden), dtype=torch.bfloat16, device=device)
+        _expect(output, "output", (T, hidden), None)
+        if output.dtype not in (torch.bfloat16, torch.float32):
+            raise TypeError(f"output must be bfloat16 or float32, got {output.dtype}")
+    elif output is not None:
+        raise ValueError("give either output or region_output")
+    if region_counts is not None:
+        _expect(region_counts, "region_counts", (region_counts.numel(),), torch.int32)
+        if region_tokens <= 0 or T % region_tokens or T // region_tokens > _lib.EP_MAX_RANKS:
+            raise ValueError(f"{T} tokens do not form at most {_lib.EP_MAX_RANKS} regions of "
+                             f"{region_tokens}")
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device)
+        if workspace is None:
+            ws, lay = workspace_for(device, T, e_local, hidden, inter, stream)
+        else:
+            lay = _lib.workspace_layout(T, e_local, hidden, inter)
+            ws = workspace
+        a = FmoeArgs()
+        a.hidden_states = hidden_states.data_ptr()
+        a.hidden_states_scale = hidden_states_scale.data_ptr()
+        a.gemm1_weights = gemm1_weights.data_ptr()
+        a.gemm1_weights_scale = gemm1_weights_scale.data_ptr()
+        a.gemm2_weights = gemm2_weights.data_ptr()
+        a.gemm2_weights_scale = gemm2_weights_scale.data_ptr()
+        a.num_tokens, a.hidden_size, a.intermediate_size = T, hidden, inter
+        a.num_experts, a.num_local_experts = E_GLOBAL, e_local
+        a.top_k, a.n_group, a.topk_group = TOP_K, N_GROUP, TOPK_GROUP
+        a.local_expert_offset = int(local_expert_offset)
+        a.routed_scaling_factor = 1.0
+        a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+        a.topk_ids, a.topk_weights = topk_ids.data_ptr(), topk_weights.data_ptr()
+        if region_counts is not None:
+            a.region_counts, a.region_tokens = region_counts.data_ptr(), int(region_tokens)
+        if phase_events is not None:
+            handles = (ctypes.c_void_p * len(phase_events))(*[e.cuda_event for e in phase_events])
+            a.phase_events = ctypes.cast(handles, ctypes.c_void_p)
+            a.num_phase_events = len(phase_events)
+        if region_output is not None:
+            a.output_dtype = _lib.OUT_F16S
+            for r, addr in enumerate(region_output):
+                a.region_output[r] = int(addr)
+        else:
+            a.output = output.data_ptr()
+            a.output_dtype = _lib.OUT_F32 if output.dtype == torch.float32 else _lib.OUT_BF16
+        rc = _lib.load().fmoe_run(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream))
+    _lib.check(rc, "fmoe_run (pre-routed)")
+    return output
 
 
 @torch.no_grad()

@@ -52,6 +52,13 @@ extern "C" {
 /* output dtypes */
 #define FMOE_OUT_BF16    0
 #define FMOE_OUT_F32     1
+/* Partial rows for expert parallelism: each token's row is H fp16 values followed by H/256
+ * fp32 power-of-two scales (value = fp16 * scale of its 256-column block), padded to a multiple
+ * of 32 bytes (the rows are written with 32-byte stores): FMOE_EP_ROW_BYTES(H) bytes at the row
+ * address that FmoeArgs.region_output gives for the token (32-byte aligned). */
+#define FMOE_OUT_F16S    2
+#define FMOE_EP_ROW_BYTES(H) (((size_t)(H) * 2 + (size_t)(H) / 256 * 4 + 31) / 32 * 32)
+#define FMOE_EP_MAX_RANKS 8
 
 /* dtype tags for the routing inputs */
 #define FMOE_DTYPE_F32   0
@@ -128,6 +135,21 @@ typedef struct FmoeArgs {
   int32_t output_dtype;
   /* FMOE_ROUTING_*; 0 (DeepSeek-V3) for callers that zero the struct. */
   int32_t routing_method;
+  /* Pre-routed calls (the receiving side of expert parallelism; NULL for a normal call). When
+   * topk_ids is set, the routing step is skipped: token t's picks are the GLOBAL expert ids
+   * topk_ids[t*8 .. t*8+8) (-1 = no pick) with weights topk_weights[t*8 ..] (device arrays),
+   * exactly as the routing of the sending rank produced them; routing_logits and routing_bias
+   * are not read. With region_counts set as well, the T tokens form T / region_tokens regions
+   * of region_tokens tokens (one per sending rank) and token j of region r takes part only if
+   * j < region_counts[r] (a device array; the other tokens are ignored). */
+  const int32_t* topk_ids;
+  const float* topk_weights;
+  const int32_t* region_counts;
+  int32_t region_tokens;
+  /* FMOE_OUT_F16S only: token j of region r is written to region_output[r] + j *
+   * FMOE_EP_ROW_BYTES(H) (32-byte aligned device addresses; may be another GPU's memory mapped
+   * into this process). Tokens without a local pick are not written. */
+  void* region_output[FMOE_EP_MAX_RANKS];
 } FmoeArgs;
 
 /* Offsets (bytes from the workspace base) of the regions tests and tools read back. */
@@ -223,9 +245,76 @@ FMOE_API int fmoe_route_permute_noalloc(const void* routing_logits, int32_t logi
 FMOE_API int fmoe_quantize_activations(const void* x_bf16, int32_t num_tokens, int32_t hidden_size,
                                        void* q_e4m3, float* scale_t, void* cuda_stream);
 
+/* ---------------------------------------------------------------- expert parallelism
+ * One rank of R (R <= FMOE_EP_MAX_RANKS) owns experts [rank*256/R, (rank+1)*256/R) and
+ * T_rank tokens. The reference's per-rank contract is run() over the local expert range
+ * (kernel.py:442-452); these entry points move tokens to the ranks that own their picks and the
+ * partial outputs back, with plain stores into the other GPUs' memory (CUDA IPC mappings, no
+ * multicast) -- no counterpart in the reference, which has no multi-GPU code.
+ *
+ * Every rank holds one device buffer of the layout below (allocate it with fmoe_ep_alloc so it
+ * can be exported, then map every other rank's buffer with fmoe_ipc_open):
+ *   recv_hidden  e4m3 [R * cap, H]     rows sent to this rank, region r = sender r
+ *   recv_scale   fp32 [H/128, R * cap] their 128-column scales (scale-major, as run() reads)
+ *   recv_ids     int32 [R * cap, 8]    the sender's routing picks (global ids) ...
+ *   recv_weights fp32 [R * cap, 8]     ... and weights
+ *   recv_counts  int32 [R]             tokens received from each sender
+ *   ret_rows     [R * cap] rows of FMOE_EP_ROW_BYTES(H): partial outputs returned to this
+ *                rank, region d = from rank d, row = the token's slot at d
+ * with cap = the most tokens any rank processes per call (a sender may send all its tokens to
+ * one rank); every rank uses the same cap, so the regions sit at the same offsets everywhere. */
+typedef struct FmoeEpLayout {
+  size_t total_bytes;
+  size_t recv_hidden, recv_scale, recv_ids, recv_weights, recv_counts, ret_rows;
+  int64_t cap;
+  size_t row_bytes;
+} FmoeEpLayout;
+
+FMOE_API int fmoe_ep_layout(int32_t world, int32_t capacity, int32_t hidden_size,
+                            FmoeEpLayout* layout);
+
+/* Device memory that other processes can map (cudaMalloc; fmoe_run itself never allocates). */
+FMOE_API int fmoe_ep_alloc(size_t bytes, void** ptr);
+FMOE_API int fmoe_ep_free(void* ptr);
+/* CUDA IPC: a 64-byte handle of an fmoe_ep_alloc buffer, and its mapping in another process
+ * (peer access enabled on first use). fmoe_ipc_close unmaps. */
+FMOE_API int fmoe_ipc_get_handle(const void* ptr, void* handle64);
+FMOE_API int fmoe_ipc_open(const void* handle64, void** ptr);
+FMOE_API int fmoe_ipc_close(void* ptr);
+
+/* Dispatch on the sending rank: for each of its T_rank tokens (picks topk_ids/topk_weights
+ * [T_rank, 8] from fmoe_route), the ranks that own at least one pick; the token's slot at such
+ * a rank is its position among this rank's tokens sent there (tokens ascending). Writes the
+ * token's e4m3 row, scales, picks and weights into region `rank` of every destination's buffer
+ * (peer_buffers[d]: rank d's buffer as mapped here, this rank's own buffer at d == rank), the
+ * per-destination count into their recv_counts[rank], and token_dest_slot [T_rank, R] (-1 = not
+ * sent) for the reduction. tokens <= capacity (the cap of fmoe_ep_layout). A system-scope fence
+ * ends the kernels; the caller then orders the destinations after them (a collective on every
+ * rank's stream). peer_buffers is a host array of `world` device addresses. */
+FMOE_API int fmoe_ep_dispatch(const int32_t* topk_ids, const float* topk_weights,
+                              const void* hidden_states, const float* hidden_states_scale,
+                              int32_t tokens, int32_t capacity, int32_t hidden_size,
+                              int32_t world, int32_t rank, void* const* peer_buffers,
+                              int32_t* token_dest_slot, void* cuda_stream);
+
+/* Reduction on the sending rank, after every destination's fmoe_run (FMOE_OUT_F16S into region
+ * `rank` of this rank's ret_rows): out[t] = bf16(sum over d = 0..R-1 of the partial row from d),
+ * in ascending rank order (= ascending expert order, the single-GPU sum order), fp32 sums. */
+FMOE_API int fmoe_ep_reduce(const int32_t* token_dest_slot, const void* buffer, int32_t tokens,
+                            int32_t capacity, int32_t hidden_size, int32_t world,
+                            void* output_bf16, void* cuda_stream);
+
 /* Copies the device status word into *status (synchronises the stream). Non-zero means a
  * kernel gave up on a bounded wait and its outputs are not valid. */
 FMOE_API int fmoe_read_status(const void* workspace, void* cuda_stream, int32_t* status);
+
+/* The device's dense FP8 tensor rate with the GEMMs' MMA shape (no counterpart in the
+ * reference): one CTA per SM issues k_blocks x 4 tcgen05.mma kind::f8f6f4 M=128 N=256 K=32 from
+ * shared memory, nothing else. Enqueued on the stream (time it with events around the call);
+ * *flops receives the FLOPs it performs; a bounded wait that ran out sets bit 0 of the device
+ * word *status. k_blocks: 1..500000. */
+FMOE_API int fmoe_fp8_mma_peak(int32_t k_blocks, int32_t* status, double* flops,
+                               void* cuda_stream);
 
 /* Number of SMs the persistent GEMM kernels size their grid for on the current device. */
 FMOE_API int fmoe_device_sm_count(int32_t* sms);

@@ -110,3 +110,48 @@ def test_run_requires_cuda_tensors():
             torch.zeros(T, 7168).to(torch.float8_e4m3fn), torch.zeros(56, T),
             torch.zeros(1, 4096, 7168, dtype=torch.float8_e4m3fn), torch.zeros(1, 32, 56),
             torch.zeros(1, 7168, 2048, dtype=torch.float8_e4m3fn), torch.zeros(1, 56, 16), 0, 2.5)
+
+
+def test_ep_layout_and_host_checks():
+    """Expert-parallel buffer layout (256-byte aligned regions in order, rows of fp16 + scales)
+    and the host-side argument checks of the dispatch and reduction entry points."""
+    lib = _lib.load()
+    for world, cap in ((2, 8192), (8, 2048), (4, 1)):
+        lay = _lib.ep_layout(world, cap, 7168)
+        offs = [lay.recv_hidden, lay.recv_scale, lay.recv_ids, lay.recv_weights, lay.recv_counts,
+                lay.ret_rows]
+        assert offs == sorted(offs) and all(o % 256 == 0 for o in offs)
+        n = world * cap
+        assert lay.recv_scale >= n * 7168 and lay.cap == cap
+        assert lay.row_bytes == _lib.ep_row_bytes(7168) == 14464  # 7168 * 2 + 28 * 4, to 32 B
+        assert lay.row_bytes % 32 == 0 and lay.ret_rows % 32 == 0
+        assert lay.total_bytes >= lay.ret_rows + n * lay.row_bytes
+    peers = (ctypes.c_void_p * 2)(None, None)
+    H = 7168
+    assert lib.fmoe_ep_dispatch(None, None, None, None, 4, 4, H, 3, 0, peers, None, None) == -2
+    assert lib.fmoe_ep_dispatch(None, None, None, None, 8, 4, H, 2, 0, peers, None, None) == -2
+    assert lib.fmoe_ep_dispatch(None, None, None, None, 4, 4, H, 2, 2, peers, None, None) == -2
+    assert lib.fmoe_ep_dispatch(None, None, None, None, 4, 4, H, 2, 0, peers, None, None) == -1
+    assert lib.fmoe_ep_reduce(None, None, 4, 2, H, 2, None, None) == -2
+    assert lib.fmoe_ep_reduce(None, None, 2, 2, H, 9, None, None) == -2
+    assert lib.fmoe_ep_layout(9, 16, H, ctypes.byref(_lib.FmoeEpLayout())) == -2
+
+
+def test_pre_routed_argument_checks():
+    """Partial-row output and token regions are only accepted for pre-routed calls, and the
+    regions must tile the tokens (at most one region per rank)."""
+    lib = _lib.load()
+    a = _lib.FmoeArgs()
+    a.num_tokens, a.hidden_size, a.intermediate_size = 8, 7168, 2048
+    a.num_experts, a.num_local_experts, a.top_k, a.n_group, a.topk_group = 256, 32, 8, 8, 4
+    a.logits_dtype, a.bias_dtype = 0, 1
+    a.output_dtype = _lib.OUT_F16S
+    assert lib.fmoe_run(ctypes.byref(a), None) == -6        # partial rows need given picks
+    a.output_dtype = _lib.OUT_BF16
+    a.region_counts, a.region_tokens = 16, 4                # any non-NULL address
+    assert lib.fmoe_run(ctypes.byref(a), None) == -2        # regions need given picks
+    a.topk_ids, a.topk_weights = 16, 16
+    a.region_tokens = 3
+    assert lib.fmoe_run(ctypes.byref(a), None) == -2        # 8 tokens are not regions of 3
+    a.region_tokens, a.num_tokens = 1, 9
+    assert lib.fmoe_run(ctypes.byref(a), None) == -2        # 9 regions > 8 ranks

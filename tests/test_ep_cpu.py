@@ -1,6 +1,8 @@
-"""Expert-parallel dispatch/combine on CPU ranks (gloo), the numpy oracle standing in for the
-CUDA kernels: the gathered EP output must equal the single-process oracle over all 256 experts.
-Small hidden/intermediate sizes keep all 256 experts' weights cheap; routing is the real one."""
+"""Expert-parallel dispatch/combine on CPU ranks (gloo, the collective transport), the numpy
+oracle standing in for the CUDA kernels: the gathered EP output must equal the single-process
+oracle over all 256 experts. Small hidden/intermediate sizes keep all 256 experts' weights cheap;
+routing is the real one. The dispatch plan (``plan_dispatch``) is the restatement the CUDA dispatch
+kernel is checked against on the GPU."""
 import os
 import socket
 
@@ -11,7 +13,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from flashinfer_b200 import workload as wl
-from flashinfer_b200.ep import ExpertParallelMoE, pack_records, plan_dispatch, unpack_records
+from flashinfer_b200.ep import ExpertParallelMoE, plan_dispatch
 from oracle import moe as omoe
 from oracle import routing as orouting
 
@@ -38,15 +40,15 @@ def _np_weights(w1, s1, w2, s2):
 
 
 def _route_oracle(logits, bias, rsf):
-    ids, _ = orouting.route(logits.float().numpy(), bias.float().numpy(), rsf)
-    return torch.from_numpy(ids)
-
-
-def _local_oracle(logits, bias, hs, sc, w1, s1, w2, s2, local_offset, rsf, out):
     ids, w = orouting.route(logits.float().numpy(), bias.float().numpy(), rsf)
+    return torch.from_numpy(ids), torch.from_numpy(w)
+
+
+def _local_oracle(ids, w, hs, sc, w1, s1, w2, s2, local_offset, out):
+    """The receiver's pre-routed operator: the sender's picks and weights, local experts only."""
     W1, S1, W2, S2 = _np_weights(w1, s1, w2, s2)
-    res = omoe.moe_reference(hs.view(torch.uint8).numpy(), sc.numpy(), W1, S1, W2, S2, ids, w,
-                             local_offset, return_f32=True)
+    res = omoe.moe_reference(hs.view(torch.uint8).numpy(), sc.numpy(), W1, S1, W2, S2,
+                             ids.numpy(), w.numpy(), local_offset, return_f32=True)
     out.copy_(torch.from_numpy(res))
 
 
@@ -60,7 +62,8 @@ def _worker(rank, world, port, hot, q):
         rows = slice(rank * per, (rank + 1) * per)
         epr = 256 // world
         w1, s1, w2, s2 = _weights(range(rank * epr, (rank + 1) * epr))
-        ep = ExpertParallelMoE(route_fn=_route_oracle, local_fn=_local_oracle)
+        ep = ExpertParallelMoE(transport="collective", hidden=H, route_fn=_route_oracle,
+                           local_fn=_local_oracle)
         out = ep.forward(act.routing_logits[rows].contiguous(), act.routing_bias,
                          act.hidden_states[rows].contiguous(),
                          act.hidden_states_scale[:, rows].contiguous(), w1, s1, w2, s2, RSF)
@@ -101,16 +104,27 @@ def test_ep_matches_single_process_oracle(world, hot):
     assert sent == len(owners)
 
 
-def test_pack_unpack_roundtrip_and_dispatch_plan():
-    act = wl.make_activations(10, 5, hidden=H)
+def test_dispatch_plan_slots():
     ids = torch.tensor([[0, 40, 200, 255, 1, 2, 3, 4]] * 10, dtype=torch.int32)
     ids[3] = torch.tensor([64, 65, 66, 67, 68, 69, 70, 71])
-    send_tok, counts = plan_dispatch(ids, 64, 4)
+    slots, counts = plan_dispatch(ids, 64, 4)
     assert counts.tolist() == [9, 1, 0, 9]
-    assert send_tok.tolist()[:9] == [0, 1, 2, 4, 5, 6, 7, 8, 9]
-    buf = pack_records(send_tok, act.routing_logits, act.hidden_states.view(torch.uint8),
-                       act.hidden_states_scale)
-    lg, hs, sc = unpack_records(buf, H)
-    assert torch.equal(lg, act.routing_logits[send_tok])
-    assert torch.equal(hs.view(torch.uint8), act.hidden_states.view(torch.uint8)[send_tok])
-    assert torch.equal(sc, act.hidden_states_scale[:, send_tok])
+    # rank 0 and 3 receive every token but token 3, in token order; rank 1 only token 3
+    assert slots[:, 0].tolist() == [0, 1, 2, -1, 3, 4, 5, 6, 7, 8]
+    assert slots[:, 1].tolist() == [-1, -1, -1, 0, -1, -1, -1, -1, -1, -1]
+    assert slots[:, 2].tolist() == [-1] * 10
+    assert slots[:, 3].tolist() == slots[:, 0].tolist()
+
+
+def test_dispatch_plan_matches_definition_on_real_routing():
+    """Every (token, owner rank) pair once; slots are ranks among the tokens sent there."""
+    act = wl.make_activations(300, 9)
+    ids, _ = orouting.route(act.routing_logits.numpy(), act.routing_bias.float().numpy(), RSF)
+    for world in (2, 4, 8):
+        epr = 256 // world
+        slots, counts = plan_dispatch(torch.from_numpy(ids), epr, world)
+        for d in range(world):
+            sent = [t for t in range(300) if any(int(e) // epr == d for e in ids[t])]
+            assert counts[d] == len(sent)
+            assert [int(slots[t, d]) for t in sent] == list(range(len(sent)))
+            assert all(int(slots[t, d]) == -1 for t in set(range(300)) - set(sent))
