@@ -619,7 +619,10 @@ def ep_arm(args):
         fp8_peak_sus = fp8["sustained_tflops"]
         flops = int(ids.size) * wl.flops_per_pair()
         nbytes = 256 * wl.bytes_per_expert() + T_EP * wl.bytes_per_token() + 512
-        launches = (7 if world == 1 else 11) * args.steps * world
+        # our kernels per step and rank: N=1 -- route, histogram (256 local experts: routing over
+        # every SM, then the per-block counts), scan, scatter, gather, GEMM1, GEMM2, combine;
+        # N>1 -- route, dispatch plan + send, the pre-routed operator's 7, reduce
+        launches = (8 if world == 1 else 11) * args.steps * world
         result = {
             "metric": METRIC, "value": round(T_EP / (ms * 1e-3), 1), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -740,6 +743,48 @@ def profile_once(args):
     summaries capture); an expert-parallel workload runs at N=1 (all 256 experts local)."""
     device = torch.device("cuda", 0)
     torch.cuda.set_device(0)
+    if args.workload.startswith("quant_t"):
+        # input quantisation (fmoe_quantize_activations) of a seeded bf16 batch of T tokens
+        T = int(args.workload[len("quant_t"):])
+        g = torch.Generator().manual_seed(T)
+        x = torch.randn(T, wl.HIDDEN, generator=g).to(torch.bfloat16).to(device)
+        for _ in range(args.warmup + 1):
+            fmoe.quantize_activations(x)
+        torch.cuda.synchronize()
+        return
+    if args.workload == "ep_dispatch":
+        # the expert-parallel data plane at full width on one GPU: 2 ranks of the configs[4] batch
+        # emulated as 2 buffers of this GPU (route, dispatch into both, reduce from both); the
+        # partial rows the reduction reads are whatever the buffers hold (traffic, not values)
+        world, per = 2, T_EP // 2
+        lay = _lib.ep_layout(world, per, wl.HIDDEN)
+        bufs = [torch.zeros(lay.total_bytes, dtype=torch.uint8, device=device) for _ in range(world)]
+        peers = (ctypes.c_void_p * world)(*[b.data_ptr() for b in bufs])
+        act, _, _ = ep_inputs("ep", 1, 0, torch.device("cpu"))
+        lib = _lib.load()
+        stream = ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+        p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+        ranks = []
+        for r in range(world):
+            rows = slice(r * per, (r + 1) * per)
+            ranks.append([t.to(device) for t in (act.routing_logits[rows].contiguous(),
+                                                 act.routing_bias,
+                                                 act.hidden_states[rows].contiguous(),
+                                                 act.hidden_states_scale[:, rows].contiguous())])
+        tds = [torch.empty((per, world), dtype=torch.int32, device=device) for _ in range(world)]
+        outs = [torch.empty((per, wl.HIDDEN), dtype=torch.bfloat16, device=device)
+                for _ in range(world)]
+        for _ in range(args.warmup + 1):
+            for r in range(world):
+                lg, b, hs, sc = ranks[r]
+                ids, w = fmoe.route(lg, b, wl.RSF_DEFAULT)
+                _lib.check(lib.fmoe_ep_dispatch(p(ids), p(w), p(hs), p(sc), per, per, wl.HIDDEN,
+                                                world, r, peers, p(tds[r]), stream), "dispatch")
+            for r in range(world):
+                _lib.check(lib.fmoe_ep_reduce(p(tds[r]), p(bufs[r]), per, per, wl.HIDDEN, world,
+                                              p(outs[r]), stream), "reduce")
+        torch.cuda.synchronize()
+        return
     if args.workload in EP_WORKLOADS:
         ws = [wl.expert_weights(e, device="cuda") for e in range(256)]
         weights = tuple(torch.stack([w[i] for w in ws]) for i in range(4))
@@ -796,7 +841,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="ep",
-                    help="ep (configs[4], the headline) | ep_hot | one of the single-GPU configs")
+                    help="ep (configs[4], the headline) | ep_hot | one of the single-GPU configs "
+                         "| quant_t<T> | ep_dispatch (--profile only: the input quantisation "
+                         "kernel; the expert-parallel dispatch and reduction on one GPU)")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-triton", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")

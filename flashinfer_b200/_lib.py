@@ -52,7 +52,8 @@ EXPORTS = ("fmoe_workspace_size", "fmoe_workspace_layout", "fmoe_run", "fmoe_rou
            "fmoe_read_status", "fmoe_device_sm_count", "fmoe_version",
            "fmoe_route_permute_noalloc", "fmoe_quantize_activations", "fmoe_ep_layout",
            "fmoe_ep_alloc", "fmoe_ep_free", "fmoe_ipc_get_handle", "fmoe_ipc_open",
-           "fmoe_ipc_close", "fmoe_ep_dispatch", "fmoe_ep_reduce", "fmoe_fp8_mma_peak")
+           "fmoe_ipc_close", "fmoe_ep_dispatch", "fmoe_ep_reduce", "fmoe_fp8_mma_peak",
+           "fmoe_debug_arm_timeout")
 
 
 class FmoeArgs(Structure):
@@ -148,6 +149,7 @@ def load() -> ctypes.CDLL:
     lib.fmoe_ep_reduce.argtypes = [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                    c_void_p, c_void_p]
     lib.fmoe_fp8_mma_peak.argtypes = [c_int32, c_void_p, POINTER(ctypes.c_double), c_void_p]
+    lib.fmoe_debug_arm_timeout.argtypes = [c_int32, ctypes.c_uint64]
     lib.fmoe_version.restype = c_char_p
     for name in EXPORTS:
         if name != "fmoe_version":

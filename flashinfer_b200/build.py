@@ -47,15 +47,22 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _stale():
         return LIB
     os.makedirs(LIBDIR, exist_ok=True)
-    objs = []
+    objs, cmds = [], []
     for src in SOURCES:
         obj = os.path.join(LIBDIR, src.replace(".cu", ".o"))
         cmd = [nvcc(), *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj]
         if verbose:
             cmd.append("-Xptxas=-v")
             print(" ".join(cmd), flush=True)
-        subprocess.run(cmd, check=True)
+        cmds.append(cmd)
         objs.append(obj)
+    # the translation units are independent: compile them side by side
+    from concurrent.futures import ThreadPoolExecutor
+    with ThreadPoolExecutor(max_workers=min(len(cmds), os.cpu_count() or 1)) as pool:
+        for r in list(pool.map(lambda c: subprocess.run(c, capture_output=not verbose), cmds)):
+            if r.returncode != 0:
+                raise RuntimeError(f"nvcc failed ({' '.join(r.args)}):\n"
+                                   f"{(r.stderr or b'').decode(errors='replace')}")
     tmp = LIB + ".tmp"
     cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-cudart", "static",
            *objs, "-o", tmp]

@@ -178,12 +178,28 @@ int validate(const FmoeArgs* a) {
   return FMOE_OK;
 }
 
+// One-shot failure-path injection armed by fmoe_debug_arm_timeout for this host thread's next
+// fmoe_run.
+struct ArmedTimeout {
+  int gemm = 0;
+  unsigned long long wait_ns = 0;
+};
+thread_local ArmedTimeout g_armed;
+
 }  // namespace
 }  // namespace fmoe
 
 using namespace fmoe;
 
 extern "C" {
+
+int fmoe_debug_arm_timeout(int32_t gemm, uint64_t wait_ns) {
+  if (gemm != 1 && gemm != 2) return FMOE_ERR_SHAPE;
+  if (wait_ns < 100000ull || wait_ns > 2000000000ull) return FMOE_ERR_SHAPE;
+  g_armed.gemm = gemm;
+  g_armed.wait_ns = wait_ns;
+  return FMOE_OK;
+}
 
 const char* fmoe_version(void) { return "flashinfer_b200 fmoe 0.1 (sm_100a, tcgen05)"; }
 
@@ -383,6 +399,9 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   p.region_tokens = a->region_counts ? a->region_tokens : T;
   p.out_mode = a->output_dtype;
   for (int r = 0; r < FMOE_EP_MAX_RANKS; ++r) p.region_out[r] = a->region_output[r];
+  p.inject_gemm = g_armed.gemm;
+  p.wait_ns = g_armed.wait_ns;
+  g_armed = ArmedTimeout{};
   p.ws = static_cast<uint8_t*>(a->workspace);
   p.L = L;
   p.num_sms = d.sms;

@@ -67,6 +67,10 @@ struct GemmArgs {
   int E, H, I;
   int64_t cap;
   int partial_rows;
+  // every bounded wait of the pipeline gives up after wait_ns of global time; inject != 0 makes
+  // the MMA warp wait on a barrier nothing arrives on (tests of the failure path only)
+  unsigned long long wait_ns;
+  int inject;
 };
 
 template <int KIND>
@@ -128,6 +132,7 @@ struct alignas(16) GemmTail {
   uint64_t tfull[4];   // [half g * 2 + buffer b]
   uint64_t tempty[4];
   uint64_t drain;
+  uint64_t never;  // armed, never arrived on: the injected wait of a failure-path test
   uint32_t tmem_base;
   int last_flag;
   int abort_flag;
@@ -185,7 +190,7 @@ __device__ __forceinline__ Unit decode_unit(int unit, int S, int NT, int nkb, co
 // the non-suspending test_wait: this wait sits on the MMA <-> epilogue hand-off, the pipeline's
 // critical path.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
-                                              volatile int* abort_flag) {
+                                              volatile int* abort_flag, uint64_t limit_ns) {
   if (mbar_test_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   uint32_t spins = 0;
@@ -193,7 +198,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
     if (mbar_test_wait(bar, parity)) return true;
     if ((++spins & 255u) == 0) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > FMOE_WAIT_NS) return false;
+      if (global_timer_ns() - t0 > limit_ns) return false;
     }
   }
 }
@@ -201,12 +206,12 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity,
 // The same for a thread that is not on the critical path (the TMA producers): each poll may
 // park the thread for up to 2 us, leaving its issue slots to the epilogue warps.
 __device__ __forceinline__ bool wait_or_abort_parked(uint64_t* bar, uint32_t parity,
-                                                     volatile int* abort_flag) {
+                                                     volatile int* abort_flag, uint64_t limit_ns) {
   const uint64_t t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait_sleep(bar, parity, 2000u)) return true;
     if (*abort_flag) return false;
-    if (global_timer_ns() - t0 > FMOE_WAIT_NS) return false;
+    if (global_timer_ns() - t0 > limit_ns) return false;
   }
 }
 
@@ -228,13 +233,13 @@ __device__ __forceinline__ float exchange_amax(GemmTail* tail, int g, int r, flo
 // warpgroup's warp, which is half a K block ahead or behind): 1-3% faster than spinning on
 // test_wait here.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                          int /*lane*/) {
+                                          uint64_t limit_ns) {
   bool got = true;
   if (!mbar_try_wait(bar, parity)) {
     const uint64_t t0 = global_timer_ns();
     while (true) {
       if (mbar_try_wait(bar, parity)) break;
-      if (*abort_flag || global_timer_ns() - t0 > FMOE_WAIT_NS) {
+      if (*abort_flag || global_timer_ns() - t0 > limit_ns) {
         got = false;
         break;
       }
@@ -335,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   GemmTail* tail = reinterpret_cast<GemmTail*>(smem + NS * STAGE + kSaRing * kSaBytes);
   float* xbuf = reinterpret_cast<float*>(tail + 1);  // [kXSmall][kXRow]
   volatile int* abort_flag = &tail->abort_flag;
+  const uint64_t wait_ns = args.wait_ns;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -356,6 +362,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tail->tempty[i], kEpiWarps / 2 * 32);  // every lane of the half's warpgroup
     }
     mbar_init(&tail->drain, 1);
+    mbar_init(&tail->never, 1);
     tail->abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_a0);
@@ -426,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // This producer issued iteration it - 2 after the release of it - 2 - NS, and the MMA
           // warp releases in order, so round r - 2 of this stage is already released: the empty
           // barrier is at most one phase behind and the parity wait is unambiguous.
-          if (r > 0 && !wait_or_abort_parked(&tail->empty[s], (r & 1) ^ 1, abort_flag)) {
+          if (r > 0 && !wait_or_abort_parked(&tail->empty[s], (r & 1) ^ 1, abort_flag, wait_ns)) {
             raise_abort(tail, args.status, kErr);
             ok = false;
             break;
@@ -466,7 +473,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_e4m3_f32(128, 128);
       int it = 0, kt = 0;
-      bool ok = true;
+      // failure-path test: a wait on a barrier nothing arrives on runs out, and the CTA takes
+      // the abort path below (status bit, producers stop and drain, TMEM freed)
+      bool ok = args.inject == 0 || wait_or_abort(&tail->never, 0, abort_flag, wait_ns);
       for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
         const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
         for (int kb = u.kb0; kb < u.kb1 && ok; ++kb, ++it, ++kt) {
@@ -474,7 +483,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int r = it / NS;
           const int b = kt & 1;
           const int rb = kt >> 1;
-          if (!wait_or_abort(&tail->full[s], r & 1, abort_flag)) {
+          if (!wait_or_abort(&tail->full[s], r & 1, abort_flag, wait_ns)) {
             ok = false;
             break;
           }
@@ -483,7 +492,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int g = 0; g < 2; ++g) {
             // half g's buffer b was released by warpgroup g two K blocks ago
-            if (rb > 0 && !wait_or_abort(&tail->tempty[g * 2 + b], (rb & 1) ^ 1, abort_flag)) {
+            if (rb > 0 &&
+                !wait_or_abort(&tail->tempty[g * 2 + b], (rb & 1) ^ 1, abort_flag, wait_ns)) {
               ok = false;
               break;
             }
@@ -566,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) continue;
         const int b = kt & 1;
         const int rb = kt >> 1;
-        if (!warp_wait(&tail->tfull[g * 2 + b], rb & 1, abort_flag, lane)) {
+        if (!warp_wait(&tail->tfull[g * 2 + b], rb & 1, abort_flag, wait_ns)) {
           if (lane == 0) raise_abort(tail, args.status, kErr);
           ok = false;
           continue;
@@ -926,6 +936,8 @@ static GemmArgs gemm_args(const RunParams& p) {
   a.I = p.I;
   a.cap = L.cap;
   a.partial_rows = static_cast<int>(L.partial_rows);
+  a.wait_ns = p.wait_ns != 0 ? p.wait_ns : FMOE_WAIT_NS;
+  a.inject = p.inject_gemm == (KIND == 1 ? 1 : 2) ? 1 : 0;
   return a;
 }
 

@@ -125,6 +125,10 @@ struct RunParams {
   int region_tokens;
   int out_mode;                // FMOE_OUT_*
   void* region_out[FMOE_EP_MAX_RANKS];
+  // failure-path test (fmoe_debug_arm_timeout): GEMM 1 or 2 waits on a barrier nothing arrives
+  // on, every GEMM wait limited to wait_ns (0 = the default limit)
+  int inject_gemm;
+  unsigned long long wait_ns;
   // workspace
   uint8_t* ws;
   Layout L;

@@ -289,7 +289,7 @@ __device__ __forceinline__ void store_picks(int32_t* ids_out, float* w_out, int 
 template <typename TL, typename TB>
 __global__ void __launch_bounds__(256) k_route(const TL* __restrict__ logits,
                                                const TB* __restrict__ bias, int T, float rsf,
-                                               int32_t* __restrict__ ids_out,
+                                               int mode, int32_t* __restrict__ ids_out,
                                                float* __restrict__ w_out) {
   pdl_begin();
   const int lane = threadIdx.x & 31;
@@ -300,8 +300,8 @@ __global__ void __launch_bounds__(256) k_route(const TL* __restrict__ logits,
   for (int t = warp0; t < T; t += nwarps) {
     int ids[kTopK];
     float w[kTopK];
-    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, kRouteDeepSeek,
-                    lane, ids, w);
+    route_token<TL>(logits + static_cast<size_t>(t) * kExpertsGlobal, b, rsf, mode, lane, ids,
+                    w);
     if (lane == 0) store_picks(ids_out, w_out, t, ids, w);
   }
 }
@@ -347,13 +347,13 @@ __global__ void __launch_bounds__(256) k_route_hist(const TL* __restrict__ logit
 // Pre-routed calls (expert parallelism): the picks come from the sending rank's routing. Block
 // b copies its tokens' picks into the workspace tables -- a token outside its region's count
 // gets no picks (-1 / 0) -- and counts its local picks per expert, like k_route_hist.
-__global__ void __launch_bounds__(256) k_hist_given(const int32_t* __restrict__ in_ids,
-                                                    const float* __restrict__ in_w,
+// With copy == 0 the picks are already the workspace tables (routed by k_route just before):
+// the block only counts them.
+__global__ void __launch_bounds__(256) k_hist_given(const int32_t* in_ids, const float* in_w,
                                                     const int32_t* __restrict__ region_counts,
                                                     int region_tokens, int T, int tpb,
-                                                    int local_start, int E,
-                                                    int32_t* __restrict__ ids_out,
-                                                    float* __restrict__ w_out,
+                                                    int local_start, int E, int copy,
+                                                    int32_t* ids_out, float* w_out,
                                                     int32_t* __restrict__ block_hist) {
   __shared__ int hist[kMaxLocalExperts];
   pdl_begin();
@@ -371,18 +371,20 @@ __global__ void __launch_bounds__(256) k_hist_given(const int32_t* __restrict__ 
     const float4* wp = reinterpret_cast<const float4*>(in_w + static_cast<size_t>(t) * kTopK);
     int4 i0 = make_int4(-1, -1, -1, -1), i1 = i0;
     float4 w0 = make_float4(0.f, 0.f, 0.f, 0.f), w1 = w0;
-    if (valid) {
-      i0 = __ldg(ip);
-      i1 = __ldg(ip + 1);
-      w0 = __ldg(wp);
-      w1 = __ldg(wp + 1);
+    if (valid) {  // plain loads: with copy == 0 the previous kernel wrote these tables
+      i0 = ip[0];
+      i1 = ip[1];
+      w0 = wp[0];
+      w1 = wp[1];
     }
-    int4* io = reinterpret_cast<int4*>(ids_out + static_cast<size_t>(t) * kTopK);
-    float4* wo = reinterpret_cast<float4*>(w_out + static_cast<size_t>(t) * kTopK);
-    io[0] = i0;
-    io[1] = i1;
-    wo[0] = w0;
-    wo[1] = w1;
+    if (copy) {
+      int4* io = reinterpret_cast<int4*>(ids_out + static_cast<size_t>(t) * kTopK);
+      float4* wo = reinterpret_cast<float4*>(w_out + static_cast<size_t>(t) * kTopK);
+      io[0] = i0;
+      io[1] = i1;
+      wo[0] = w0;
+      wo[1] = w1;
+    }
     const int ids[kTopK] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
@@ -405,19 +407,19 @@ cudaError_t launch_route(const void* logits, int logits_dtype, const void* bias,
   if (logits_dtype == FMOE_DTYPE_F32 && bias_dtype == FMOE_DTYPE_BF16)
     (void)launch_pdl(k_route<float, __nv_bfloat16>, grid, block, 0, s,
         static_cast<const float*>(logits), static_cast<const __nv_bfloat16*>(bias), T, rsf,
-        topk_ids, topk_w);
+        kRouteDeepSeek, topk_ids, topk_w);
   else if (logits_dtype == FMOE_DTYPE_F32 && bias_dtype == FMOE_DTYPE_F32)
     (void)launch_pdl(k_route<float, float>, grid, block, 0, s, static_cast<const float*>(logits),
                                                   static_cast<const float*>(bias), T, rsf,
-                                                  topk_ids, topk_w);
+                                                  kRouteDeepSeek, topk_ids, topk_w);
   else if (logits_dtype == FMOE_DTYPE_BF16 && bias_dtype == FMOE_DTYPE_BF16)
     (void)launch_pdl(k_route<__nv_bfloat16, __nv_bfloat16>, grid, block, 0, s,
         static_cast<const __nv_bfloat16*>(logits), static_cast<const __nv_bfloat16*>(bias), T,
-        rsf, topk_ids, topk_w);
+        rsf, kRouteDeepSeek, topk_ids, topk_w);
   else
     (void)launch_pdl(k_route<__nv_bfloat16, float>, grid, block, 0, s,
         static_cast<const __nv_bfloat16*>(logits), static_cast<const float*>(bias), T, rsf,
-        topk_ids, topk_w);
+        kRouteDeepSeek, topk_ids, topk_w);
   return cudaGetLastError();
 }
 
@@ -860,6 +862,30 @@ cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s) {
   if (p.T <= 0) return cudaSuccess;
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
+  if (L.nblocks < p.num_sms) {
+    // Few routing blocks (many local experts: at most 8,192 per-block counts): routing in the
+    // fused kernel would run on nblocks CTAs only, so the tokens are routed by a grid over every
+    // SM (one warp per token) and the blocks then count the picks from the workspace tables.
+    cudaError_t e = dispatch_dtypes(p.logits_dtype, p.bias_dtype, [&](auto tl, auto tb) {
+      using TL = decltype(tl);
+      using TB = decltype(tb);
+      int blocks = (p.T + 7) / 8;
+      if (blocks > p.num_sms * 16) blocks = p.num_sms * 16;
+      (void)launch_pdl(k_route<TL, TB>, blocks, 256, 0, s, static_cast<const TL*>(p.logits),
+                       static_cast<const TB*>(p.bias), p.T, p.rsf, p.route_mode,
+                       reinterpret_cast<int32_t*>(ws + L.topk_ids),
+                       reinterpret_cast<float*>(ws + L.topk_w));
+      return cudaGetLastError();
+    });
+    if (e != cudaSuccess) return e;
+    auto* ids = reinterpret_cast<int32_t*>(ws + L.topk_ids);
+    auto* w = reinterpret_cast<float*>(ws + L.topk_w);
+    (void)launch_pdl(k_hist_given, L.nblocks, 256, 0, s, static_cast<const int32_t*>(ids),
+                     static_cast<const float*>(w), static_cast<const int32_t*>(nullptr), p.T,
+                     p.T, L.tpb, p.local_start, p.E, 0, ids, w,
+                     reinterpret_cast<int32_t*>(ws + L.block_hist));
+    return cudaGetLastError();
+  }
   return dispatch_dtypes(p.logits_dtype, p.bias_dtype, [&](auto tl, auto tb) {
     using TL = decltype(tl);
     using TB = decltype(tb);
@@ -876,7 +902,7 @@ cudaError_t launch_hist_given(const RunParams& p, cudaStream_t s) {
   uint8_t* ws = p.ws;
   const Layout& L = p.L;
   (void)launch_pdl(k_hist_given, L.nblocks, 256, 0, s, p.in_ids, p.in_w, p.region_counts,
-                   p.region_tokens, p.T, L.tpb, p.local_start, p.E,
+                   p.region_tokens, p.T, L.tpb, p.local_start, p.E, 1,
                    reinterpret_cast<int32_t*>(ws + L.topk_ids),
                    reinterpret_cast<float*>(ws + L.topk_w),
                    reinterpret_cast<int32_t*>(ws + L.block_hist));

@@ -304,6 +304,14 @@ FMOE_API int fmoe_ep_reduce(const int32_t* token_dest_slot, const void* buffer, 
                             int32_t capacity, int32_t hidden_size, int32_t world,
                             void* output_bf16, void* cuda_stream);
 
+/* Failure-path test (no counterpart in the reference): arms the next fmoe_run of the calling
+ * host thread so that GEMM `gemm` (1 or 2) waits on a barrier nothing arrives on, with every wait
+ * of that call's GEMMs limited to wait_ns (100 us .. 2 s) instead of 2 s. The wait runs out, the
+ * kernel sets FMOE_STATUS_TIMEOUT_GEMM<gemm> in the status word, stops its producers, waits for
+ * its copies in flight, frees its tensor memory and returns; the call's output is not valid, and
+ * the next call runs normally (its plan kernel clears the status word). One-shot. */
+FMOE_API int fmoe_debug_arm_timeout(int32_t gemm, uint64_t wait_ns);
+
 /* Copies the device status word into *status (synchronises the stream). Non-zero means a
  * kernel gave up on a bounded wait and its outputs are not valid. */
 FMOE_API int fmoe_read_status(const void* workspace, void* cuda_stream, int32_t* status);
