@@ -4,7 +4,7 @@
 # nor pyproject.toml, so its solution tree and config are copied as they are. bench.py's Triton
 # timing leg imports baseline/_ref/solution/triton/kernel.py::run from here.
 set -e
-SRC=${1:-/root/reference}
+SRC=${1:?usage: install_ref.sh <reference checkout>}
 DST=$(dirname "$0")/_ref
 [ -d "$SRC/solution" ] || { echo "no reference at $SRC" >&2; exit 1; }
 rm -rf "$DST"
