@@ -64,24 +64,6 @@ bool make_tmap_u8(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// 4-D uint8 tensor map over the weights for the GEMMs' half tiles: dims {cols, rows_per_block,
-// 2, outer} with strides {cols, rows_per_block * cols, 2 * rows_per_block * cols} bytes (a plain
-// reshape of the row-major weights, no overlap), box {128, 64, 2, 1}, 128-byte swizzle: one load
-// gives rows [r, r+64) of two consecutive blocks as one 128-row K-major tile.
-bool make_tmap_u8_halves(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows_per_block,
-                         uint64_t outer) {
-  EncodeTiledFn fn = get_encode_fn();
-  if (!fn) return false;
-  const cuuint64_t dims[4] = {cols, rows_per_block, 2, outer};
-  const cuuint64_t strides[3] = {cols, rows_per_block * cols, 2 * rows_per_block * cols};
-  const cuuint32_t box[4] = {128, 64, 2, 1};
-  const cuuint32_t estr[4] = {1, 1, 1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 struct DeviceInfo {
   int sms = 0;
   int major = 0;
@@ -342,12 +324,10 @@ const TensorMaps* tensor_maps(const RunParams& p, const FmoeArgs* a, const Layou
   e.valid = false;
   TensorMaps* m = &e.maps;
   if (!make_tmap_u8(&m->a, p.ws + L.a_perm, H, L.cap, H, 128, 128) ||
-      // W1 [E][2][I][H]: {K, row in gate/up block, block, expert}
-      !make_tmap_u8_halves(&m->w1, a->gemm1_weights, H, I, E) ||
+      !make_tmap_u8(&m->w1, a->gemm1_weights, H, static_cast<uint64_t>(E) * 2 * I, H, 128, 128) ||
       !make_tmap_u8(&m->hi, p.ws + L.h_hi, I, L.cap, I, 128, T <= kPackedMaxT ? 64 : 128) ||
       !make_tmap_u8(&m->lo, p.ws + L.h_lo, I, L.cap, I, 128, T <= kPackedMaxT ? 64 : 128) ||
-      // W2 [E*H/256][2][128][I]: {K, row in n-block, n-block, 256-row tile}
-      !make_tmap_u8_halves(&m->w2, a->gemm2_weights, I, 128, static_cast<uint64_t>(E) * H / 256) ||
+      !make_tmap_u8(&m->w2, a->gemm2_weights, I, static_cast<uint64_t>(E) * H, I, 128, 256) ||
       // per-K-block activation scales, [K blocks][cap] fp32: one 128-slot row per load
       !make_tmap_f32_rows(&m->sa1, p.ws + L.a_scale_t, L.cap, H / kBlock, 128) ||
       !make_tmap_f32_rows(&m->sa2, p.ws + L.h_scale_t, L.cap, I / kBlock, 128))

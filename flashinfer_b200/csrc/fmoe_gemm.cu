@@ -12,10 +12,8 @@
 //               shared-memory ring. One issuing warp sustains about 42 B/cycle per SM of
 //               128-row boxes; two sustain about 79 B/cycle, above the 48 KB per 520-cycle
 //               K block that the MMA consumes.
-//   warp 1      MMA issuer: per 128-wide K block and per half g of the tile's 256 weight rows,
-//               tcgen05.mma kind::f8f6f4 M=128 N=128 K=32 x4 (x8 for KIND 2) into half g's
-//               TMEM partial buffer b (four 128-column regions: 2 halves x 2 buffers), one
-//               commit per half.
+//   warp 1      MMA issuer: per 128-wide K block, tcgen05.mma kind::f8f6f4 M=128 N=256 K=32
+//               x4 (x8 for KIND 2) into one of two TMEM partial buffers (2 x 256 columns).
 //   warp 3      idle (completes warpgroup 0, whose register budget is handed to the epilogue).
 //   warps 4-11  promotion + epilogue: read each K block's partial from TMEM, scale it by
 //               a_scale[slot, kb] * w_scale[n-block, kb] and accumulate in fp32 registers
@@ -25,16 +23,12 @@
 // epilogue warpgroups take them (setmaxnreg.inc to 224): 168 x 384 = 56 x 128 + 224 x 256, so
 // each epilogue thread holds its 128 accumulators, two 16-column TMEM load buffers and the tile
 // end's working set without spilling in the K loop.
-// Half g of a tile holds rows [g*64, g*64+64) of both 128-row weight blocks (gate and up, or the
-// tile's two 128-row n-blocks), loaded by one 4-D TMA box {128 K, 64 rows, 2 blocks, 1}, so it
-// is a plain 128-row K-major operand; epilogue warpgroup g (warps 4+4g .. 7+4g, one per TMEM lane
-// quarter) consumes only half g. The two warpgroups are thus fed half a K block apart and each
-// has its own double buffer: the MMA for half g of K block k+2 waits only for warpgroup g's
-// release of block k, while three other half-blocks (about 768 cycles) run on the tensor core.
-// (With one 256-column buffer pair shared by all eight epilogue warps, the two warps of each SM
-// sub-partition worked in lockstep and the hand-off round trip sat on the critical path.) Waits
-// spin on mbarrier.test_wait (a suspended try_wait wakes up late) and every epilogue lane
-// arrives on its buffer-empty barrier itself.
+// The hand-offs between the MMA warp and the epilogue are the pipeline's critical path (only two
+// 256-column TMEM buffers fit in TMEM): waits spin on mbarrier.test_wait (a suspended try_wait
+// wakes up late) and every epilogue lane arrives on the buffer-empty barrier itself (no warp
+// synchronisation before the arrive). Splitting each tile's MMA into two N=128 halves with a
+// TMEM double buffer per epilogue warpgroup (so the warpgroups run half a K block apart) was
+// built and measured 10-12% slower on both GEMMs (same box, same inputs).
 // Work unit = (tile, K split). Tiles are ordered expert -> n-tile -> m-tile so concurrently
 // running CTAs share weight tiles in L2. For small batches with fewer tiles than SMs the K range
 // is split; every split writes its fp32 partial tile and k_split_finish (a separate kernel,
@@ -129,8 +123,8 @@ constexpr int xbuf_bytes() {
 struct alignas(16) GemmTail {
   uint64_t full[4];
   uint64_t empty[4];
-  uint64_t tfull[4];   // [half g * 2 + buffer b]
-  uint64_t tempty[4];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
   uint64_t drain;
   uint64_t never;  // armed, never arrived on: the injected wait of a failure-path test
   uint32_t tmem_base;
@@ -228,23 +222,10 @@ __device__ __forceinline__ float exchange_amax(GemmTail* tail, int g, int r, flo
   return fmaxf(tail->amax_x[0][r], tail->amax_x[1][r]);
 }
 
-// Every lane polls the barrier; the warp agrees on the outcome. The epilogue warps wait with
-// try_wait (a suspended warp leaves the issue slots of its SM sub-partition to the other
-// warpgroup's warp, which is half a K block ahead or behind): 1-3% faster than spinning on
-// test_wait here.
+// Every lane polls the barrier; the warp agrees on the outcome.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           uint64_t limit_ns) {
-  bool got = true;
-  if (!mbar_try_wait(bar, parity)) {
-    const uint64_t t0 = global_timer_ns();
-    while (true) {
-      if (mbar_try_wait(bar, parity)) break;
-      if (*abort_flag || global_timer_ns() - t0 > limit_ns) {
-        got = false;
-        break;
-      }
-    }
-  }
+  const bool got = wait_or_abort(bar, parity, abort_flag, limit_ns);
   return __all_sync(0xffffffffu, got);
 }
 
@@ -357,9 +338,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&tail->full[s], 1);
       mbar_init(&tail->empty[s], 1);
     }
-    for (int i = 0; i < 4; ++i) {
-      mbar_init(&tail->tfull[i], 1);
-      mbar_init(&tail->tempty[i], kEpiWarps / 2 * 32);  // every lane of the half's warpgroup
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tail->tfull[b], 1);
+      mbar_init(&tail->tempty[b], kEpiWarps * 32);  // every epilogue lane arrives
     }
     mbar_init(&tail->drain, 1);
     mbar_init(&tail->never, 1);
@@ -385,16 +366,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* st = smem + s * STAGE;
     mbar_arrive_expect_tx(&tail->full[s], STAGE + kSaBytes);
     const int kx = kb * kBlock;
-    // half g: rows [g*64, g*64+64) of the tile's two 128-row weight blocks (the map's third
-    // dimension: gate then up for GEMM1, the tile's two n-blocks for GEMM2), 16 KB, a 128-row
-    // K-major operand in shared memory. GEMM1's map is {K, row in block (I), block (2), expert},
-    // GEMM2's {K, row in n-block (128), n-block (2), 256-row tile (E * H / 256)}.
-    const int r1 = KIND == 1 ? u.n * kBlock : 0;
-    const int t3 = KIND == 1 ? u.e : u.e * (args.H / kTileN) + u.n;
-#pragma unroll
-    for (int g = 0; g < 2; ++g)
-      tma_load_4d(st + C::A_TILES * kATileBytes + g * kATileBytes, &tm_w, &tail->full[s], kx,
-                  r1 + g * 64, 0, t3, pol_w);
+    if (KIND == 1) {
+      const int wrow = u.e * 2 * args.I + u.n * kBlock;
+      tma_load_2d(st + kATileBytes, &tm_w, &tail->full[s], kx, wrow, pol_w);
+      tma_load_2d(st + 2 * kATileBytes, &tm_w, &tail->full[s], kx, wrow + args.I, pol_w);
+    } else {
+      tma_load_2d(st + C::A_TILES * kATileBytes, &tm_w, &tail->full[s], kx,
+                  u.e * args.H + u.n * kTileN, pol_w);
+    }
   };
   // Each role branch starts with its warpgroup's register change (ptxas allocates each branch
   // under the limit its setmaxnreg sets), then waits for the previous grid.
@@ -471,47 +450,38 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(128, 128);
+      constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
       int it = 0, kt = 0;
       // failure-path test: a wait on a barrier nothing arrives on runs out, and the CTA takes
       // the abort path below (status bit, producers stop and drain, TMEM freed)
       bool ok = args.inject == 0 || wait_or_abort(&tail->never, 0, abort_flag, wait_ns);
       for (int unit = blockIdx.x; unit < units && ok; unit += gridDim.x) {
         const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
-        for (int kb = u.kb0; kb < u.kb1 && ok; ++kb, ++it, ++kt) {
+        for (int kb = u.kb0; kb < u.kb1; ++kb, ++it, ++kt) {
           const int s = it % NS;
           const int r = it / NS;
           const int b = kt & 1;
           const int rb = kt >> 1;
-          if (!wait_or_abort(&tail->full[s], r & 1, abort_flag, wait_ns)) {
+          if (!wait_or_abort(&tail->full[s], r & 1, abort_flag, wait_ns) ||
+              (rb > 0 && !wait_or_abort(&tail->tempty[b], (rb & 1) ^ 1, abort_flag, wait_ns))) {
             ok = false;
             break;
           }
+          tc_fence_after();
+          const uint32_t d = tmem + b * kTileN;
           const uint32_t st = smem_u32(smem + s * STAGE);
           const uint64_t a_desc = smem_desc_k128(st);
+          const uint64_t b_desc = smem_desc_k128(st + C::A_TILES * kATileBytes);
 #pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            // half g's buffer b was released by warpgroup g two K blocks ago
-            if (rb > 0 &&
-                !wait_or_abort(&tail->tempty[g * 2 + b], (rb & 1) ^ 1, abort_flag, wait_ns)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t d = tmem + (g * 2 + b) * 128;
-            const uint64_t b_desc = smem_desc_k128(st + (C::A_TILES + g) * kATileBytes);
+          for (int j = 0; j < 4; ++j)  // 4 x K=32 covers the 128-byte row
+            mma_f8f6f4(d, a_desc + 2 * j, b_desc + 2 * j, idesc, j > 0 ? 1u : 0u);
+          if (KIND == 2) {
+            const uint64_t lo_desc = smem_desc_k128(st + kATileBytes);
 #pragma unroll
-            for (int j = 0; j < 4; ++j)  // 4 x K=32 covers the 128-byte row
-              mma_f8f6f4(d, a_desc + 2 * j, b_desc + 2 * j, idesc, j > 0 ? 1u : 0u);
-            if (KIND == 2) {
-              const uint64_t lo_desc = smem_desc_k128(st + kATileBytes);
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                mma_f8f6f4(d, lo_desc + 2 * j, b_desc + 2 * j, idesc, 1u);
-            }
-            mma_commit(&tail->tfull[g * 2 + b]);
+            for (int j = 0; j < 4; ++j) mma_f8f6f4(d, lo_desc + 2 * j, b_desc + 2 * j, idesc, 1u);
           }
-          if (ok) mma_commit(&tail->empty[s]);
+          mma_commit(&tail->empty[s]);
+          mma_commit(&tail->tfull[b]);
         }
       }
       if (!ok) raise_abort(tail, args.status, kErr);
@@ -576,19 +546,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) continue;
         const int b = kt & 1;
         const int rb = kt >> 1;
-        if (!warp_wait(&tail->tfull[g * 2 + b], rb & 1, abort_flag, wait_ns)) {
+        if (!warp_wait(&tail->tfull[b], rb & 1, abort_flag, wait_ns)) {
           if (lane == 0) raise_abort(tail, args.status, kErr);
           ok = false;
           continue;
         }
         if (warp_rows) {
           tc_fence_after();
-          const uint32_t taddr =
-              tmem + (static_cast<uint32_t>(q * 32) << 16) + (g * 2 + b) * 128;
-          // half g's 128 columns: rows g*64 + [0,64) of the gate block (or n-block 0), then of
-          // the up block (n-block 1); 8 chunks of 16, chunk c+1 in flight while c accumulates.
+          const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * kTileN;
+          // 8 chunks of 16 columns: gate (or n-block 0) cols g*64 + [0,64), then up (n-block 1)
+          // cols 128 + g*64 + [0,64). Chunk c+1 is in flight while chunk c is accumulated.
           float va[16], vb[16];
-          tmem_ld_32x32b_x16(taddr, va);
+          tmem_ld_32x32b_x16(taddr + g * 64, va);
           // the activation scale reached shared memory before the MMA that this wait follows;
           // the shared-memory reads overlap the first TMEM load
           const float sa = sa_ring[(kt % kSaRing) * 128 + prow];
@@ -598,7 +567,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 8; ++c) {
             const int cn = c + 1;
-            const int coln = cn * 16;
+            const int coln = (cn < 4 ? 0 : 128) + g * 64 + (cn & 3) * 16;
             const float f = c < 4 ? f0 : f1;
             if ((c & 1) == 0) {
               if (cn < 8) tmem_ld_32x32b_x16(taddr + coln, vb);
@@ -612,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_before();
         }
-        mbar_arrive(&tail->tempty[g * 2 + b]);
+        mbar_arrive(&tail->tempty[b]);
       }
       // w_sc[par ^ 1] was last read in the previous unit, which every epilogue thread has left
       if (has_next) store_w_scale(par ^ 1, w_next);

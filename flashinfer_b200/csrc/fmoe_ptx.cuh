@@ -111,19 +111,6 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
       : "memory");
 }
 
-// 4-D tiled bulk tensor load global -> shared (c0 innermost), completion counted in bytes on
-// `bar`.
-__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* tmap, uint64_t* bar,
-                                            int32_t c0, int32_t c1, int32_t c2, int32_t c3,
-                                            uint64_t cache_hint) {
-  asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
-      "r"(c3), "l"(cache_hint)
-      : "memory");
-}
-
 // L2 eviction-priority policies for the cache_hint operand.
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
