@@ -192,6 +192,22 @@ cudaError_t launch_route_permute(const void* logits, int logits_dtype, const voi
                                  int H, int I, int num_sms, const PermuteBuffers& b,
                                  cudaStream_t s);
 
+// ---------------------------------------------------------------- output stores
+// Eight fp32 values of an output row as bf16 (round to nearest even) or fp32; v counts groups of
+// eight columns.
+__device__ __forceinline__ void store8(__nv_bfloat16* out, size_t v, const float (&acc)[8]) {
+  uint4 o;
+  __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) oh[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+  reinterpret_cast<uint4*>(out)[v] = o;
+}
+__device__ __forceinline__ void store8(float* out, size_t v, const float (&acc)[8]) {
+  float4* o = reinterpret_cast<float4*>(out) + 2 * v;
+  o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+
 // ---------------------------------------------------------------- 256-bit global accesses
 __device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&w)[8]) {
   asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(w[0]), "r"(w[1]),

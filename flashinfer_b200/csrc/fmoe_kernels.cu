@@ -1022,18 +1022,6 @@ cudaError_t launch_route_permute(const void* logits, int logits_dtype, const voi
 // Y rows are fp16 with a power-of-two scale per 256 columns (exact to apply). Tokens without
 // local picks get zeros (kernel.py:692-695 zero-fills when nothing is local).
 // ------------------------------------------------------------------------------------------
-__device__ __forceinline__ void store8(__nv_bfloat16* out, size_t v, const float (&acc)[8]) {
-  uint4 o;
-  __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) oh[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
-  reinterpret_cast<uint4*>(out)[v] = o;
-}
-__device__ __forceinline__ void store8(float* out, size_t v, const float (&acc)[8]) {
-  float4* o = reinterpret_cast<float4*>(out) + 2 * v;
-  o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-  o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-}
 
 // Each thread owns 32 consecutive output columns (inside one 256-column scale tile) of one
 // token: per local pick it issues both 32-byte loads of the y row at once (64 bytes in flight);
