@@ -112,7 +112,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // The weight boxes of iteration it (K block kb of unit u) into stage s, with the stage's
   // transaction count for the whole stage (weights, activations and activation scales).
-  auto issue_weights = [&](int s, const Unit& u, int kb, uint64_t pol_w) {
+  // L2 policy of a weight box: an expert with more than 128 routed rows has several m-tiles,
+  // whose units (consecutive, so on CTAs running side by side) all stream the same weight tile,
+  // so its boxes are kept (evict_last); otherwise a box is read once and goes first
+  // (evict_first), leaving L2 to the activations. With evict_first everywhere the headline
+  // batch (T=16384 over 256 experts, ~4 m-tiles per expert) read its weights from DRAM 2.7
+  // times per GEMM; the per-expert choice took GEMM1 from 5.36 to 4.75 ms there and left the
+  // one-m-tile batches unchanged.
+  auto issue_weights = [&](int s, const Unit& u, int kb, uint64_t pol_first, uint64_t pol_last) {
+    const uint64_t pol_w = tail->ecnt[u.e] > kTileM ? pol_last : pol_first;
     uint8_t* st = smem + s * STAGE;
     mbar_arrive_expect_tx(&tail->full[s], STAGE + kSaBytes);
     const int kx = kb * kBlock;
@@ -131,12 +139,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
     if ((warp == 0 || warp == kProducer2Warp) && lane == 0) {
       const int pw = warp == 0 ? 0 : 1;
-      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_first = policy_evict_first();
+      const uint64_t pol_last = policy_evict_last();
       int it = 0;
       for (int unit = blockIdx.x; unit < units && it < NS; unit += gridDim.x) {
         const Unit u = decode_unit(unit, S, NT, nkb, tail->ebase, tail->ecnt, E);
         for (int kb = u.kb0; kb < u.kb1 && it < NS; ++kb, ++it)
-          if ((it & 1) == pw) issue_weights(it, u, kb, pol_w);
+          if ((it & 1) == pw) issue_weights(it, u, kb, pol_first, pol_last);
       }
     }
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -146,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------------ TMA producers
     const int pw = warp == 0 ? 0 : 1;  // issues the K iterations it with (it & 1) == pw
     if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();
+      const uint64_t pol_first = policy_evict_first();
       const uint64_t pol_a = policy_evict_last();
       int last_round[NS];
 #pragma unroll
@@ -168,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* st = smem + s * STAGE;
-          if (it >= NS) issue_weights(s, u, kb, pol_w);  // else issued before the wait
+          if (it >= NS) issue_weights(s, u, kb, pol_first, pol_a);  // else issued before the wait
           const int kx = kb * kBlock;
           tma_load_2d(sa_ring + (it % kSaRing) * 128, &tm_sa, &tail->full[s], u.row0, kb, pol_a);
           if (KIND == 1) {
