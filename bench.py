@@ -41,7 +41,7 @@ EP_WORKLOADS = {"ep": ("uniform logits", 10, 0.0), "ep_hot": ("hot group 0 (+1.5
 
 METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
 SMALL_T = 64           # T <= SMALL_T: fused route/plan/scatter cluster kernel
-SPLIT_MAX_T = 32       # T <= SPLIT_MAX_T: split-K finish kernel after each GEMM
+SPLIT_MAX_T = 8        # T <= SPLIT_MAX_T: split-K finish kernel after each GEMM
 
 
 def kernels_per_call(T: int) -> int:

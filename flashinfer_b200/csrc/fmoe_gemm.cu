@@ -691,12 +691,13 @@ static cudaError_t launch_gemm_kind(const RunParams& p, const CUtensorMap& a0,
 }
 
 cudaError_t launch_split_finish(const RunParams& p, int kind, cudaStream_t s) {
-  // at most partial_rows (<= kSplitMaxT) rows of 256 fp32 per tile in shared memory
+  // at most partial_rows (<= kSplitMaxT) rows of 256 fp32 per tile in shared memory; two CTAs
+  // per SM, so up to 2 * num_sms split tiles (T=8: 160 GEMM1 tiles) finish in one round
   const size_t smem = static_cast<size_t>(p.L.partial_rows) * kTileN * 4;
   if (kind == 1)
-    (void)launch_pdl(k_split_finish<1>, p.num_sms, 256, smem, s, gemm_args<1>(p));
+    (void)launch_pdl(k_split_finish<1>, 2 * p.num_sms, 256, smem, s, gemm_args<1>(p));
   else
-    (void)launch_pdl(k_split_finish<2>, p.num_sms, 256, smem, s, gemm_args<2>(p));
+    (void)launch_pdl(k_split_finish<2>, 2 * p.num_sms, 256, smem, s, gemm_args<2>(p));
   return cudaGetLastError();
 }
 

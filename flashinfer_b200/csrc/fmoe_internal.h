@@ -143,9 +143,14 @@ cudaError_t launch_route_hist(const RunParams& p, cudaStream_t s);
 cudaError_t launch_scan(const RunParams& p, cudaStream_t s);
 cudaError_t launch_scatter_gather(const RunParams& p, cudaStream_t s);
 cudaError_t launch_gather(const RunParams& p, cudaStream_t s);
-// Split-K (GEMM units over K ranges) only for T <= kSplitMaxT, where a call has fewer tiles than
-// SMs; the split partial tiles are finished by launch_split_finish(kind) after each GEMM.
-constexpr int kSplitMaxT = 32;
+// Split-K (GEMM units over K ranges) only for T <= kSplitMaxT, where a call can have fewer tiles
+// than SMs; the split partial tiles are finished by launch_split_finish(kind) after each GEMM.
+// The finish launch itself costs about 4 us even when the plan picks no split: its CTAs wait for
+// the whole GEMM1 grid, so GEMM2's CTAs no longer start (and prefetch weights) as GEMM1's CTAs
+// leave. At 16 <= T <= 32 the plan had picked no split anyway (8-9 active experts, 128-144 GEMM1
+// tiles): T=16 83.1 -> 79.9 us and T=32 86.1 -> 83.1 us without the launch; at T=8 the split is
+// worth it (99.9 us with it, 114.8 without).
+constexpr int kSplitMaxT = 8;
 cudaError_t launch_split_finish(const RunParams& p, int kind, cudaStream_t s);
 // T <= kSmallT: routing + histogram + plan + scatter in one kernel (replaces the three above):
 // one CTA (one warp per token) per 8 tokens, up to 8 CTAs in one cluster exchanging counts

@@ -301,6 +301,29 @@ def test_small_batch_one_hot_expert(T, gpu_weights, cpu_weights):
     assert frac == 1.0, (frac, err)
 
 
+@pytest.mark.parametrize("T", [4, 8])
+def test_split_tiles_with_several_rows(T, gpu_weights, cpu_weights):
+    """Every token picks local experts 5, 6, 7 and global experts 40-44 (outside the 32 local
+    ones): GEMM1 has 48 tiles of T rows each, fewer than the SMs, so the plan splits their K
+    range and k_split_finish sums T-row partial tiles. Every output row against the oracle."""
+    act = wl.make_activations(T, 700 + T)
+    act.routing_logits[:, 5:8] += 30.0
+    act.routing_logits[:, 40:45] += 30.0
+    act.routing_bias[5:8] = 1.0
+    act.routing_bias[40:45] = 1.0
+    cfg = wl.Config(f"split_t{T}", T, 700 + T)
+    out, ws, lay = run_gpu(act, gpu_weights, cfg)
+    view = fmoe.WorkspaceView(ws, lay, T, 32, wl.HIDDEN, wl.INTER)
+    counts = view.expert_count().cpu().numpy()
+    assert list(np.nonzero(counts)[0]) == [5, 6, 7] and np.all(counts[5:8] == T)
+    plan = view.plan().cpu().numpy()
+    assert plan[3] > 1, plan  # plan word 3: GEMM1's K splits per tile
+    bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
+    ref = oracle_rows(act, cfg, np.arange(T), cpu_weights)
+    frac, err = omoe.allclose_report(bits, ref, atol=ATOL, rtol=RTOL)
+    assert frac == 1.0, (frac, err)
+
+
 def test_output_written_in_place(gpu_weights):
     cfg = wl.CONFIGS["t8_s2"]
     act = cfg.activations()
