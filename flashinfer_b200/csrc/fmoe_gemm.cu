@@ -53,8 +53,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(NS >= 2 && NS <= 4, "barrier arrays hold 4 stages; alternating producers need 2");
   constexpr int STAGE = C::STAGE;
   constexpr int kErr = KIND == 1 ? FMOE_STATUS_TIMEOUT_GEMM1 : FMOE_STATUS_TIMEOUT_GEMM2;
-  // Until griddepcontrol.wait below, the previous kernel may still run: its predecessor-ordered
-  // launch (pdl_begin_in_order) guarantees only that the plan and the expert tables are complete.
+  // Until griddepcontrol.wait below, the previous kernel may still run. The plan and the expert
+  // tables are complete: the gather releases GEMM1 only after its own wait (pdl_begin_in_order),
+  // and GEMM2 starts after GEMM1 has.
   // The prologue and the weight loads of the first NS K iterations, which need nothing else,
   // run before the wait; the activations are loaded after it.
 
@@ -539,9 +540,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 // loads in flight -- then runs the tile's epilogue with one warp per valid row: SwiGLU and the
 // two-term e4m3 encoding (KIND 1) or fp16 with a power-of-two scale (KIND 2), the same
 // arithmetic as k_gemm's register epilogue.
+// Dependents are released before the wait: GEMM2 reads the plan before its own wait, and the
+// plan was complete before GEMM1 launched (the gather releases GEMM1 only after its own wait),
+// so GEMM2 may start and prefetch weights while this kernel waits for GEMM1; GEMM2's wait then
+// covers this kernel, which ends after GEMM1. T=8: 99.1 -> 98.4 us per call.
 template <int KIND>
 __global__ void __launch_bounds__(256) k_split_finish(const GemmArgs args) {
-  pdl_begin_in_order();  // GEMM2, which follows, reads the plan before its own wait
+  pdl_begin();
   const int S = args.plan[KIND == 1 ? kPlanSplit1 : kPlanSplit2];
   if (S <= 1) return;
   const int tiles = args.plan[KIND == 1 ? kPlanTiles1 : kPlanTiles2];
