@@ -42,12 +42,16 @@ EP_WORKLOADS = {"ep": ("uniform logits", 10, 0.0), "ep_hot": ("hot group 0 (+1.5
 METRIC = json.load(open(os.path.join(ROOT, "BASELINE.json")))["metric"]
 SMALL_T = 64           # T <= SMALL_T: fused route/plan/scatter cluster kernel
 SPLIT_MAX_T = 8        # T <= SPLIT_MAX_T: split-K finish kernel after each GEMM
+GEMV_MAX_T = _lib.GEMV_MAX_T  # T <= GEMV_MAX_T: plan kernel + two matrix-vector kernels
 
 
 def kernels_per_call(T: int) -> int:
     """Launches of one call: route+hist, scan, scatter, gather, gemm1, gemm2, combine; for
-    T <= SMALL_T the fused plan kernel replaces the first three, and for T <= SPLIT_MAX_T a
-    split-K finish kernel follows each GEMM."""
+    T <= SMALL_T the fused plan kernel replaces the first three, for T <= SPLIT_MAX_T a split-K
+    finish kernel follows each GEMM, and for T <= GEMV_MAX_T the call is the plan kernel and the
+    two matrix-vector kernels."""
+    if T <= GEMV_MAX_T:
+        return 3
     if T <= SPLIT_MAX_T:
         return 7
     if T <= SMALL_T:

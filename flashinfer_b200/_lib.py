@@ -42,6 +42,8 @@ def ep_row_bytes(hidden: int) -> int:
     padded to a multiple of 32 bytes."""
     return (hidden * 2 + hidden // 256 * 4 + 31) // 32 * 32
 STOP_NONE, STOP_ROUTE, STOP_GATHER, STOP_GEMM1, STOP_GEMM2 = 0, 1, 2, 3, 4
+PATH_AUTO, PATH_GEMM = 0, 1
+GEMV_MAX_T = 2  # calls of at most this many tokens take the matrix-vector path (PATH_AUTO)
 # FMOE_ROUTING_* (include/fmoe.h)
 (ROUTING_DEEPSEEK_V3, ROUTING_DEFAULT, ROUTING_RENORMALIZE, ROUTING_LLAMA4,
  ROUTING_RENORMALIZE_NAIVE, ROUTING_TOPK) = range(6)
@@ -91,6 +93,7 @@ class FmoeArgs(Structure):
         ("region_counts", c_void_p),
         ("region_tokens", c_int32),
         ("region_output", c_void_p * EP_MAX_RANKS),
+        ("gemm_path", c_int32),
     ]
 
 

@@ -16,8 +16,8 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
 LIBDIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(LIBDIR, "libfmoe.so")
-SOURCES = ["fmoe_api.cu", "fmoe_kernels.cu", "fmoe_gemm.cu", "fmoe_static.cu", "fmoe_quant.cu",
-           "fmoe_ep.cu", "fmoe_peak.cu"]
+SOURCES = ["fmoe_api.cu", "fmoe_kernels.cu", "fmoe_gemm.cu", "fmoe_gemv.cu", "fmoe_static.cu",
+           "fmoe_quant.cu", "fmoe_ep.cu", "fmoe_peak.cu"]
 HEADERS = ["fmoe_internal.h", "fmoe_ptx.cuh", "fmoe_gemm_common.cuh",
            os.path.join("..", "..", "include", "fmoe.h")]
 

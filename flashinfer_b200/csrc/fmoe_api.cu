@@ -125,6 +125,7 @@ int validate(const FmoeArgs* a) {
   if (a->local_expert_offset < 0 ||
       a->local_expert_offset + a->num_local_experts > a->num_experts)
     return FMOE_ERR_OFFSET;
+  if (a->gemm_path != FMOE_PATH_AUTO && a->gemm_path != FMOE_PATH_GEMM) return FMOE_ERR_SHAPE;
   const bool pre_routed = a->topk_ids != nullptr;
   if ((!pre_routed && ((a->logits_dtype != FMOE_DTYPE_F32 && a->logits_dtype != FMOE_DTYPE_BF16) ||
                        (a->bias_dtype != FMOE_DTYPE_F32 && a->bias_dtype != FMOE_DTYPE_BF16))) ||
@@ -363,7 +364,9 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
   p.bias_dtype = a->bias_dtype;
   p.hidden = static_cast<const uint8_t*>(a->hidden_states);
   p.hidden_scale = a->hidden_states_scale;
+  p.w1 = static_cast<const uint8_t*>(a->gemm1_weights);
   p.w1_scale = a->gemm1_weights_scale;
+  p.w2 = static_cast<const uint8_t*>(a->gemm2_weights);
   p.w2_scale = a->gemm2_weights_scale;
   p.output = a->output;
   p.T = T;
@@ -399,6 +402,12 @@ int fmoe_run(const FmoeArgs* a, void* stream_ptr) {
     if (launch_scatter_gather(p, s) != cudaSuccess || !mark(2)) return FMOE_ERR_CUDA;
   } else if (T <= kSmallT) {
     if (launch_plan_small(p, s) != cudaSuccess || !mark(1)) return FMOE_ERR_CUDA;
+    if (a->gemm_path == FMOE_PATH_AUTO && a->stop_after == FMOE_STOP_NONE && gemv_eligible(p)) {
+      // small batch: GEMM1 + SwiGLU, then GEMM2 + combine, as matrix-vector kernels
+      if (!mark(2) || launch_gemv(p, 1, s) != cudaSuccess || !mark(3)) return FMOE_ERR_CUDA;
+      if (launch_gemv(p, 2, s) != cudaSuccess || !mark(4) || !mark(5)) return FMOE_ERR_CUDA;
+      return FMOE_OK;
+    }
     if (launch_gather(p, s) != cudaSuccess || !mark(2)) return FMOE_ERR_CUDA;
   } else {
     if (launch_route_hist(p, s) != cudaSuccess || launch_scan(p, s) != cudaSuccess || !mark(1))

@@ -112,7 +112,9 @@ struct RunParams {
   int bias_dtype;
   const uint8_t* hidden;
   const float* hidden_scale;   // [H/128, T]
+  const uint8_t* w1;           // [E, 2I, H] e4m3
   const float* w1_scale;       // [E, 2I/128, H/128]
+  const uint8_t* w2;           // [E, H, I] e4m3
   const float* w2_scale;       // [E, H/128, I/128]
   void* output;                // [T, H] bf16, or fp32 (out_mode FMOE_OUT_F32)
   int T, H, I, E, local_start;
@@ -152,6 +154,15 @@ cudaError_t launch_gather(const RunParams& p, cudaStream_t s);
 // worth it (99.9 us with it, 114.8 without).
 constexpr int kSplitMaxT = 8;
 cudaError_t launch_split_finish(const RunParams& p, int kind, cudaStream_t s);
+// T <= kGemvMaxT (fmoe_gemv.cu): after the plan kernel, GEMM1 + SwiGLU and GEMM2 + the combine as
+// weight-streaming matrix-vector kernels on the CUDA cores (launch_gemv(p, 1), then 2), for calls
+// that gemv_eligible accepts (plain routed calls with a bf16 or fp32 output). Same-box graph
+// timings against the grouped GEMMs: T=1 (one active expert) 29.7 -> 21.7 us, T=2 13.8 -> 10.4;
+// with three or more active experts the grouped GEMMs stream weights faster (T=3: 59.0 vs 66.3,
+// T=4: 46.2 vs 45.9, T=8: 98.8 vs 148.3).
+constexpr int kGemvMaxT = 2;
+bool gemv_eligible(const RunParams& p);
+cudaError_t launch_gemv(const RunParams& p, int which, cudaStream_t s);
 // T <= kSmallT: routing + histogram + plan + scatter in one kernel (replaces the three above):
 // one CTA (one warp per token) per 8 tokens, up to 8 CTAs in one cluster exchanging counts
 // through distributed shared memory

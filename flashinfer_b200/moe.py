@@ -65,7 +65,8 @@ def _launch(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
             gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
             routed_scaling_factor, output, stop_after: int = _lib.STOP_NONE,
             workspace: Optional[torch.Tensor] = None,
-            routing_method: int = _lib.ROUTING_DEEPSEEK_V3, top_k: int = TOP_K):
+            routing_method: int = _lib.ROUTING_DEEPSEEK_V3, top_k: int = TOP_K,
+            gemm_path: int = _lib.PATH_AUTO):
     T = int(routing_logits.shape[0])
     e_local = int(gemm1_weights.shape[0])
     hidden = int(hidden_states.shape[1])
@@ -125,6 +126,7 @@ def _launch(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
         a.workspace = ws.data_ptr()
         a.workspace_bytes = ws.numel()
         a.stop_after = int(stop_after)
+        a.gemm_path = int(gemm_path)
         a.output_dtype = _lib.OUT_F32 if output.dtype == torch.float32 else _lib.OUT_BF16
         a.routing_method = int(routing_method)
         rc = _lib.load().fmoe_run(ctypes.byref(a), ctypes.c_void_p(stream.cuda_stream))

@@ -83,6 +83,9 @@ extern "C" {
 #define FMOE_ROUTING_TOPK              5
 
 /* Stop points for staged execution (tests inspect the workspace in between). */
+#define FMOE_PATH_AUTO     0
+#define FMOE_PATH_GEMM     1
+
 #define FMOE_STOP_NONE     0
 #define FMOE_STOP_ROUTE    1   /* after routing, permutation and the activation gather */
 #define FMOE_STOP_GATHER   2   /* same point (the gather is fused into the permutation) */
@@ -150,6 +153,11 @@ typedef struct FmoeArgs {
    * FMOE_EP_ROW_BYTES(H) (32-byte aligned device addresses; may be another GPU's memory mapped
    * into this process). Tokens without a local pick are not written. */
   void* region_output[FMOE_EP_MAX_RANKS];
+  /* FMOE_PATH_AUTO (0): calls of at most 2 tokens with a bf16 or fp32 output run the
+   * matrix-vector path (GEMM1 and GEMM2 streamed on the CUDA cores, SwiGLU and the combine fused
+   * in; 3 kernels); FMOE_PATH_GEMM: always the grouped tensor-core GEMMs. Staged calls
+   * (stop_after != 0) always take the grouped GEMMs. */
+  int32_t gemm_path;
 } FmoeArgs;
 
 /* Offsets (bytes from the workspace base) of the regions tests and tools read back. */

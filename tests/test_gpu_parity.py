@@ -42,11 +42,11 @@ def oracle_rows(act, cfg, rows, cpu_weights, local_start=0, e_local=32):
     return omoe.moe_reference(hs, sc, W1, s1, W2, s2, ids, w, local_start)
 
 
-def run_gpu(act, gpu_weights, cfg, local_start=0, stop=_lib.STOP_NONE):
+def run_gpu(act, gpu_weights, cfg, local_start=0, stop=_lib.STOP_NONE, path=_lib.PATH_AUTO):
     lg, b, hs, sc = to_gpu(act)
     w1, s1, w2, s2 = gpu_weights
     out, ws, lay = fmoe._launch(lg, b, hs, sc, w1, s1, w2, s2, local_start, cfg.rsf, None,
-                                stop_after=stop)
+                                stop_after=stop, gemm_path=path)
     torch.cuda.synchronize()
     assert fmoe.read_status(ws) == 0
     return out, ws, lay
@@ -109,11 +109,18 @@ def test_permutation_bit_exact(name, local_start, gpu_weights):
             assert base[e] <= s < base[e] + counts[e] and slot_tok[s] == t
 
 
-@pytest.mark.parametrize("name", sorted(FULL_OUTPUT))
-def test_output_matches_oracle_and_golden(name, gpu_weights, cpu_weights, golden_outputs):
+# The smallest calls run the matrix-vector path by default; PATH_GEMM keeps the grouped
+# tensor-core GEMMs covered at the same sizes.
+SMALL_PATHS = [(n, p) for n in sorted(FULL_OUTPUT) for p in
+               ([_lib.PATH_AUTO, _lib.PATH_GEMM] if wl.CONFIGS[n].T <= _lib.GEMV_MAX_T
+                else [_lib.PATH_AUTO])]
+
+
+@pytest.mark.parametrize("name,path", SMALL_PATHS)
+def test_output_matches_oracle_and_golden(name, path, gpu_weights, cpu_weights, golden_outputs):
     cfg = wl.CONFIGS[name]
     act = cfg.activations()
-    out, _, _ = run_gpu(act, gpu_weights, cfg)
+    out, _, _ = run_gpu(act, gpu_weights, cfg, path=path)
     bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
     rows = FULL_OUTPUT[name] or cfg.T
     sel = np.arange(rows)
@@ -301,27 +308,45 @@ def test_small_batch_one_hot_expert(T, gpu_weights, cpu_weights):
     assert frac == 1.0, (frac, err)
 
 
-@pytest.mark.parametrize("T", [4, 8])
-def test_split_tiles_with_several_rows(T, gpu_weights, cpu_weights):
+@pytest.mark.parametrize("T,path", [(4, _lib.PATH_GEMM), (8, _lib.PATH_GEMM), (1, _lib.PATH_AUTO),
+                                    (2, _lib.PATH_AUTO), (2, _lib.PATH_GEMM)])
+def test_split_tiles_with_several_rows(T, path, gpu_weights, cpu_weights):
     """Every token picks local experts 5, 6, 7 and global experts 40-44 (outside the 32 local
-    ones): GEMM1 has 48 tiles of T rows each, fewer than the SMs, so the plan splits their K
-    range and k_split_finish sums T-row partial tiles. Every output row against the oracle."""
+    ones): T routed rows per active expert. Grouped GEMMs: GEMM1 has 48 tiles of T rows each,
+    fewer than the SMs, so the plan splits their K range and k_split_finish sums T-row partial
+    tiles. Matrix-vector path (T <= 2): a token sum over three experts in k_gemv2. Every
+    output row against the oracle."""
     act = wl.make_activations(T, 700 + T)
     act.routing_logits[:, 5:8] += 30.0
     act.routing_logits[:, 40:45] += 30.0
     act.routing_bias[5:8] = 1.0
     act.routing_bias[40:45] = 1.0
     cfg = wl.Config(f"split_t{T}", T, 700 + T)
-    out, ws, lay = run_gpu(act, gpu_weights, cfg)
+    out, ws, lay = run_gpu(act, gpu_weights, cfg, path=path)
     view = fmoe.WorkspaceView(ws, lay, T, 32, wl.HIDDEN, wl.INTER)
     counts = view.expert_count().cpu().numpy()
     assert list(np.nonzero(counts)[0]) == [5, 6, 7] and np.all(counts[5:8] == T)
     plan = view.plan().cpu().numpy()
-    assert plan[3] > 1, plan  # plan word 3: GEMM1's K splits per tile
+    if T <= 8:  # split-K only for T <= 8
+        assert plan[3] > 1, plan  # plan word 3: GEMM1's K splits per tile
     bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
     ref = oracle_rows(act, cfg, np.arange(T), cpu_weights)
     frac, err = omoe.allclose_report(bits, ref, atol=ATOL, rtol=RTOL)
     assert frac == 1.0, (frac, err)
+
+
+@pytest.mark.parametrize("name", ["t1_s1"])
+def test_small_batch_paths_agree_and_repeat(name, gpu_weights):
+    """The matrix-vector path against the grouped GEMMs on the same call (both are within the
+    oracle tolerance elsewhere; here within 1e-2 of each other), and bit-identical on a rerun."""
+    cfg = wl.CONFIGS[name]
+    act = cfg.activations()
+    gemv, _, _ = run_gpu(act, gpu_weights, cfg)
+    gemv = gemv.clone()
+    again, _, _ = run_gpu(act, gpu_weights, cfg)
+    assert torch.equal(gemv.view(torch.int16), again.view(torch.int16))
+    tc, _, _ = run_gpu(act, gpu_weights, cfg, path=_lib.PATH_GEMM)
+    torch.testing.assert_close(gemv.float(), tc.float(), atol=1e-2, rtol=1e-2)
 
 
 def test_output_written_in_place(gpu_weights):
