@@ -18,7 +18,7 @@ LIBDIR = os.path.join(PKG, "_lib")
 LIB = os.path.join(LIBDIR, "libfmoe.so")
 SOURCES = ["fmoe_api.cu", "fmoe_kernels.cu", "fmoe_gemm.cu", "fmoe_gemv.cu", "fmoe_static.cu",
            "fmoe_quant.cu", "fmoe_ep.cu", "fmoe_peak.cu"]
-HEADERS = ["fmoe_internal.h", "fmoe_ptx.cuh", "fmoe_gemm_common.cuh",
+HEADERS = ["fmoe_internal.h", "fmoe_ptx.cuh", "fmoe_gemm_common.cuh", "fmoe_route.cuh",
            os.path.join("..", "..", "include", "fmoe.h")]
 
 NVCC_FLAGS = [
