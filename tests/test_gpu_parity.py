@@ -327,20 +327,23 @@ def test_split_tiles_with_several_rows(T, path, gpu_weights, cpu_weights):
     counts = view.expert_count().cpu().numpy()
     assert list(np.nonzero(counts)[0]) == [5, 6, 7] and np.all(counts[5:8] == T)
     plan = view.plan().cpu().numpy()
-    if T <= 8:  # split-K only for T <= 8
-        assert plan[3] > 1, plan  # plan word 3: GEMM1's K splits per tile
+    assert plan[3] > 1, plan  # plan word 3: GEMM1's K splits per tile (split-K for T <= 8)
     bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
     ref = oracle_rows(act, cfg, np.arange(T), cpu_weights)
     frac, err = omoe.allclose_report(bits, ref, atol=ATOL, rtol=RTOL)
     assert frac == 1.0, (frac, err)
 
 
-@pytest.mark.parametrize("name", ["t1_s1"])
-def test_small_batch_paths_agree_and_repeat(name, gpu_weights):
+@pytest.mark.parametrize("name,logits_bf16", [("t1_s1", False), ("t1_s1", True)])
+def test_small_batch_paths_agree_and_repeat(name, logits_bf16, gpu_weights):
     """The matrix-vector path against the grouped GEMMs on the same call (both are within the
-    oracle tolerance elsewhere; here within 1e-2 of each other), and bit-identical on a rerun."""
+    oracle tolerance elsewhere; here within 1e-2 of each other), and bit-identical on a rerun;
+    also with bf16 logits and an fp32 bias."""
     cfg = wl.CONFIGS[name]
     act = cfg.activations()
+    if logits_bf16:
+        act.routing_logits = act.routing_logits.to(torch.bfloat16)
+        act.routing_bias = act.routing_bias.float()
     gemv, _, _ = run_gpu(act, gpu_weights, cfg)
     gemv = gemv.clone()
     again, _, _ = run_gpu(act, gpu_weights, cfg)

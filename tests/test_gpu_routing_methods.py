@@ -42,9 +42,10 @@ def test_method_routing_and_counts(method, top_k, gpu_weights):
     np.testing.assert_array_equal(view.expert_count().cpu().numpy(), counts)
 
 
+@pytest.mark.parametrize("T", [16, 2])  # T=2: the matrix-vector path
 @pytest.mark.parametrize("method,top_k", [(1, 8), (3, 1), (5, 3)])
-def test_method_output_matches_oracle(method, top_k, gpu_weights, cpu_weights):
-    cfg = wl.CONFIGS["t16_s0"]
+def test_method_output_matches_oracle(method, top_k, T, gpu_weights, cpu_weights):
+    cfg = wl.CONFIGS["t16_s0"] if T == 16 else wl.Config("t2_s2006", 2, 2006)
     act = cfg.activations()
     out = fmoe.run(*_gpu(act), *gpu_weights, 0, cfg.rsf, routing_method=method, top_k=top_k)
     bits = out.view(torch.int16).cpu().numpy().view(np.uint16)
